@@ -1,0 +1,355 @@
+#!/usr/bin/env python
+"""Benchmark: one 50-block MiniMax H3-shaped DiT denoising step at 37,760 tokens (BASELINE configs 3 / 4).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 --master-port P bench.py --gpus N
+
+A step = 50 EngineBlock forwards of the 37,760-token sequence (text 512 + keyframe 1,680 + audio 496 + video 35,072)
+at BASELINE's H3 shape (hidden 5120, 40 x 128 heads, GELU-tanh FFN 20480) with random N(0, 0.02) weights quantised
+to NVFP4 once at load, FP8 attention, per-token adaLN modulation.  At N > 1 the sequence is token-sharded and
+attention runs Ulysses head-parallel over NCCL (config 4; total work fixed, so scaling is "strong").
+
+Timing: W warm-up steps (the first runs on dynamic scales, later ones on delayed scales -- the reference's steady
+state), then K steps bracketed by a barrier + synchronize, timed with CUDA events on the launching stream, max over
+ranks.  Every step reads 8.9 GB of weights plus GBs of activations, far beyond the 126 MB L2.  `e2e` repeats the step
+through the public API with host buffers (pinned H2D of the step's inputs, D2H of its output, inside the timed region).
+`--impl reference` times the reference's torch path restated on the CPU (the oracle) on a bounded row sample,
+extrapolated to the full step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "minimax-h3-tensorfold-rtx_b200"
+sys.path.insert(0, str(PKG))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "s/denoise step, 50-block H3 DiT @37.8k tok, 1/2/4/8 B200; NVFP4 GEMM TFLOPS"
+SEQ = 37760
+SEGS = (512, 1680, 496, 35072)          # text | keyframe | audio | video (33 latent frames x 24 x 44 patches)
+PEAKS = ROOT / "MEASURED_PEAKS.json"
+FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def mod_segments(S: int):
+    a = np.cumsum((0,) + SEGS[:-1]).tolist()
+    segs = [(a[i], a[i] + SEGS[i], i) for i in range(3)] + [(a[3], S, 3)]
+    return segs
+
+
+def rope_3d(S: int, rot: int = 128, splits=(44, 42, 42), grid=(33, 24, 44), theta: float = 10000.0) -> torch.Tensor:
+    """ComfyUI-style rotation table [1, S, 1, rot/2, 2, 2] fp32: text / keyframe / audio tokens at t = 0..; the video
+    tokens on the (33, 24, 44) latent grid; pairs split over (t, h, w) as 22 / 21 / 21."""
+
+    half = rot // 2
+    parts = [s // 2 for s in splits]
+    s = torch.arange(S, dtype=torch.float64)
+    v0 = S - grid[0] * grid[1] * grid[2]
+    vi = (s - v0).clamp_min(0)
+    t = torch.where(s < v0, s, vi // (grid[1] * grid[2]))
+    hh = torch.where(s < v0, torch.zeros_like(s), (vi // grid[2]) % grid[1])
+    ww = torch.where(s < v0, torch.zeros_like(s), vi % grid[2])
+    angs = []
+    for pos, n in zip((t, hh, ww), parts):
+        f = theta ** (-torch.arange(n, dtype=torch.float64) / n)
+        angs.append(pos[:, None] * f[None, :])
+    ang = torch.cat(angs, 1)[:, :half]
+    c, sn = torch.cos(ang), torch.sin(ang)
+    rope = torch.stack([torch.stack([c, -sn], -1), torch.stack([sn, c], -1)], -2)
+    return rope.float().reshape(1, S, 1, half, 2, 2)
+
+
+def activations(S: int, D: int, seed: int = 0) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(S, D, generator=g)
+    ch = torch.randperm(D, generator=torch.Generator().manual_seed(2))[: D // 100]
+    x[:, ch] *= 20
+    return x.to(torch.bfloat16)
+
+
+def peaks() -> tuple[dict, str]:
+    if PEAKS.exists():
+        return json.loads(PEAKS.read_text()), "measured"
+    return FALLBACK, "fallback"
+
+
+class Clocks:
+    """nvidia-smi clock / throttle samples during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.p.wait(5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+
+    def summary(self) -> dict:
+        self.f.flush()
+        rows = [r.split(",") for r in Path(self.f.name).read_text().splitlines() if r.count(",") >= 8]
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i] and "Not" not in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][2]),
+                "samples": len(rows), "reasons": reasons}
+
+
+# ------------------------------------------------------------------------------------------------ CPU leg
+def cpu_sample(rows: int, S: int = SEQ, layers: int = 50, threads: int | None = None) -> dict:
+    """The reference's torch path restated on the CPU (oracle/): one block's work for `rows` token rows -- norm +
+    modulation, NVFP4 fake-quant of each linear input, fp32 matmuls, q/k norm + RoPE, attention of those rows against
+    all S keys, gated residuals, GELU MLP -- timed and extrapolated to S tokens x `layers` blocks."""
+
+    sys.path.insert(0, str(ROOT))
+    from oracle import block as OB
+    from oracle import nvfp4 as ON
+    from oracle import ops as OO
+
+    torch.set_num_threads(threads or os.cpu_count())
+    D, H, Dh, F = 5120, 40, 128, 20480
+    g = torch.Generator().manual_seed(0)
+    W = {n: torch.randn(s, generator=g) * 0.02 for n, s in
+         {"qkv": (3 * H * Dh, D), "out": (D, H * Dh), "fc1": (F, D), "fc2": (D, F)}.items()}
+    x = activations(rows, D).float().numpy()
+    kv = torch.randn(2, H, S, Dh, generator=g)
+    mod = (0.1 * torch.randn(4, 6, D, generator=g)).numpy()
+    idx = np.zeros(rows, dtype=np.int32)
+    rope = OB.rope_table(rows, 128)
+    w1, w2 = (1 + 0.02 * torch.randn(D, generator=g)).numpy(), (1 + 0.02 * torch.randn(Dh, generator=g)).numpy()
+
+    def lin(a, w):
+        q, s = ON.quantize(a, ON.global_scale(float(np.abs(a).max())))
+        return ON.bf16_round((torch.from_numpy(ON.dequantize(q, s, ON.global_scale(float(np.abs(a).max())))) @
+                              w.T).numpy())
+
+    t0 = time.perf_counter()
+    h = OO.norm_mod(x, w1, mod, 0, idx, 1e-5)
+    qkv = lin(h, W["qkv"])
+    q = OO.qknorm_rope(qkv[:, :H * Dh].reshape(rows, H, Dh), w2, rope, 1e-5)
+    o = torch.nn.functional.scaled_dot_product_attention(torch.from_numpy(q).transpose(0, 1), kv[0], kv[1])
+    o = ON.bf16_round(o.transpose(0, 1).reshape(rows, H * Dh).numpy())
+    xm = OO.gate_add(x, lin(o, W["out"]), mod, 0, idx)
+    a = OO.gelu_tanh(lin(OO.norm_mod(xm, w1, mod, 1, idx, 1e-5), W["fc1"]))
+    OO.gate_add(xm, lin(a, W["fc2"]), mod, 1, idx)
+    dt = time.perf_counter() - t0
+    return {"sample_s": dt, "value": dt * (S / rows) * layers, "cores": torch.get_num_threads(),
+            "sample": f"one block for {rows} of {S} token rows (attention against all {S} keys), x {S / rows:.1f} "
+                      f"rows x {layers} blocks"}
+
+
+def reference_arm(a) -> None:
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    rows = a.cpu_rows
+    for _ in range(a.warmup):
+        cpu_sample(rows)
+    vals = [cpu_sample(rows) for _ in range(a.steps)]
+    v = statistics.mean(r["value"] for r in vals)
+    line = {"metric": METRIC, "value": v, "unit": "s/step", "n_gpus": a.gpus, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": v * 1e3, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp32 (NVFP4 fake-quant)", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "config 3 step sample on the host CPU (oracle restatement of the reference's "
+                                   "torch path)", "global_batch": 1, "seq_len": SEQ, "parallelism": "cpu"},
+            "cpu_baseline": {"value": v, "unit": "s/step", "cores": vals[0]["cores"], "kind": "port",
+                             "sample": vals[0]["sample"]},
+            "e2e": {"value": v, "unit": "s/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------ GPU leg
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seq", type=int, default=SEQ)
+    ap.add_argument("--layers", type=int, default=50)
+    ap.add_argument("--cpu-rows", type=int, default=512)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-e2e", action="store_true")
+    a = ap.parse_args()
+    if a.impl == "reference":
+        return reference_arm(a)
+
+    from tfvideo import minimax_h3 as M
+    from tfvideo import native as N
+    from tfvideo.profiling import StageTimer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    group = None
+    if world > 1:
+        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=600),
+                                             device_id=torch.device("cuda", local))
+        group = torch.distributed.group.WORLD
+    cfg = M.Config(layers=a.layers, dim=5120, heads=40, head_dim=128, ffn=20480, act="gelu", t_dim=8)
+    S = a.seq
+    n = S // world
+    t0 = n * rank
+    eng = M.MiniMaxH3Engine.synthetic(cfg, seed=1, device="cuda", group=group)
+    x0 = activations(S, cfg.dim)[t0:t0 + n].cuda()
+    t_emb = torch.randn(2, cfg.t_dim, generator=torch.Generator().manual_seed(3)).cuda()
+    segs = mod_segments(S)
+    rope = rope_3d(S).cuda()
+    x = torch.empty_like(x0)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier(device_ids=[local])
+
+    def step():
+        x.copy_(x0)
+        eng.forward(x, t_emb, segs, rope)
+
+    for _ in range(max(a.warmup, 1)):
+        step()
+    torch.cuda.synchronize()
+    assert N.device_status() == 0
+    timer = StageTimer()
+    eng.timer = timer
+    barrier()
+    torch.cuda.synchronize()
+    launches0 = N.LAUNCHES
+    with Clocks(local) as clocks:
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.record()
+        for _ in range(a.steps):
+            step()
+        en.record()
+        torch.cuda.synchronize()
+        barrier()
+    launches = N.LAUNCHES - launches0
+    eng.timer = None
+    ms = st.elapsed_time(en) / a.steps
+    stages = timer.summary()
+    status = N.device_status()
+    finite = bool(torch.isfinite(x).all())
+    t = torch.tensor([ms], device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+
+    # ---- e2e through the public API: EngineBlock per block, host inputs and outputs
+    e2e = None
+    if not a.no_e2e:
+        blocks = [M.EngineBlock(eng, i) for i in range(len(eng.blocks))]
+        xh = x0.cpu().pin_memory()
+        rh = rope.cpu().pin_memory()
+        th = t_emb.cpu().pin_memory()
+        out_h = torch.empty_like(xh).pin_memory()
+        xd, rd, td = torch.empty_like(x0), torch.empty_like(rope), torch.empty_like(t_emb)
+
+        def e2e_step():
+            xd.copy_(xh, non_blocking=True)
+            rd.copy_(rh, non_blocking=True)
+            td.copy_(th, non_blocking=True)
+            sg = [tuple(s) for s in segs]           # a fresh segment list: the row index is rebuilt and uploaded
+            h = xd
+            for blk in blocks:
+                h = blk(h, td, sg, rd)
+            out_h.copy_(h, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        te = torch.tensor([e0.elapsed_time(e1) / a.steps], device="cuda")
+        if world > 1:
+            torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
+        h2d = xh.numel() * 2 + rh.numel() * 4 + th.numel() * 4 + S * 4
+        e2e = {"value": float(te.item()) / 1e3, "unit": "s/step", "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(out_h.numel() * 2)}
+
+    # ---- roofline of the dominant kernel (attention at this shape) and the GEMMs
+    pk, src = peaks()
+    sustained = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+    per_block = {k: v["ms"] / v["calls"] for k, v in stages.items()}
+    Hl = cfg.heads // world
+    attn_flops = 4.0 * S * S * Hl * cfg.head_dim
+    attn_ms = per_block.get("attention", float("nan"))
+    gemm_flops = {"gemm_qkv": 2.0 * n * 3 * cfg.inner * cfg.dim, "gemm_out+gate": 2.0 * n * cfg.dim * cfg.inner,
+                  "gemm_fc1+act+quant": 2.0 * n * cfg.ffn * cfg.dim, "gemm_fc2+gate": 2.0 * n * cfg.dim * cfg.ffn}
+    gemm_ms = sum(per_block.get(k, 0.0) for k in gemm_flops)
+    gemm_tflops = sum(gemm_flops.values()) / (gemm_ms * 1e-3) / 1e12 if gemm_ms else None
+    achieved = attn_flops / (attn_ms * 1e-3) / 1e12
+    fp8_peak = 2 * sustained
+    roofline = {"kernel": "attn_fp8 (tcgen05 FP8 flash attention incl. its prepare)", "bound": "tensor",
+                "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s", "frac": achieved / fp8_peak,
+                "traffic": None,
+                "peak_note": f"2 x {src} bf16 sustained ({sustained} TF/s): dense FP8 = 2 x bf16 on B200",
+                "work_per_launch": f"4*S^2*H*Dh = {attn_flops:.4g} FLOP (S={S}, H={Hl})",
+                "nvfp4_gemm": {"achieved": gemm_tflops, "peak": 4 * sustained, "unit": "TFLOP/s",
+                               "frac": (gemm_tflops / (4 * sustained)) if gemm_tflops else None,
+                               "peak_note": f"4 x {src} bf16 sustained: dense NVFP4 = 4 x bf16 on B200"}}
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu:
+        r = cpu_sample(a.cpu_rows)
+        cpu = {"value": r["value"], "unit": "s/step", "cores": r["cores"], "kind": "port", "sample": r["sample"],
+               "sample_seconds": r["sample_s"]}
+    if rank == 0:
+        line = {"metric": METRIC, "value": ms / 1e3, "unit": "s/step", "n_gpus": world, "steps": a.steps,
+                "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "strong",
+                "vs_baseline": None, "dtype": "nvfp4 linears / fp8-e4m3 attention, fp32 accumulate",
+                "data": "synthetic (seeded N(0,1) activations with 1% x20 outlier channels; N(0,0.02) weights)",
+                "config": {"workload": "config 3/4: 50-block H3-shaped DiT step, 37,760 tokens (512/1680/496/35072), "
+                                       "D=5120, 40x128 heads, GELU-tanh FFN 20480, NVFP4 W4A4 + FP8 attention",
+                           "global_batch": 1, "seq_len": S, "layers": cfg.layers,
+                           "parallelism": "single GPU" if world == 1 else f"ulysses sp{world} (token-sharded)",
+                           "l2": "inputs larger than L2 (8.9 GB weights + activations per step)"},
+                "stages_ms_per_step": {k: round(v["ms"] / a.steps, 3) for k, v in stages.items()},
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+                "clocks": clocks.summary(), "device_status": status, "finite": finite}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    _ = math
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,372 @@
+// libh3b200: the C ABI (include/h3b200.h) over the sm_100a kernels.  One translation unit: every kernel header is
+// included here, so the device status word and the kernels live in one module.  Host code validates arguments,
+// builds TMA tensor maps (cuTensorMapEncodeTiled, fetched from the driver at first use) and launches on the
+// caller's stream.  Nothing here allocates device memory.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "attention.cuh"
+#include "elementwise.cuh"
+#include "gemm_nvfp4.cuh"
+#include "h3b200.h"
+
+using namespace h3;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(H3_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  return H3_OK;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+cudaStream_t S_(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// ------------------------------------------------------------------------------------------------ tensor maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D byte matrix [rows, cols] (row stride `ld` bytes) read in boxes of box_cols (<= 128) x box_rows, 128-byte swizzle.
+int make_map_u8(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_cols,
+                uint32_t box_rows, const char* what) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(H3_ERR_CUDA, "%s: cuTensorMapEncodeTiled unavailable from the driver", what);
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(H3_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, (int)r);
+  return H3_OK;
+}
+
+// Opt a kernel into more than 48 KB of dynamic shared memory once per device.
+template <typename K>
+int smem_optin(K kernel, int bytes, unsigned* done_mask, const char* what) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 32 && (__atomic_load_n(done_mask, __ATOMIC_RELAXED) >> dev) & 1u) return H3_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return fail(H3_ERR_CUDA, "%s: cudaFuncSetAttribute: %s", what, cudaGetErrorString(e));
+  if (dev < 32) __atomic_fetch_or(done_mask, 1u << dev, __ATOMIC_RELAXED);
+  return H3_OK;
+}
+
+unsigned g_optin_gemm256 = 0, g_optin_gemm128 = 0, g_optin_attn = 0;
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct AttnWs {
+  size_t q8, k8, vt8, qscale, kscale, kmean, vscale, vinv, ksum, vmax, total;
+  int SP, nblk;
+};
+
+AttnWs attn_ws(int S, int H) {
+  AttnWs w;
+  w.SP = (S + 255) / 256 * 256;
+  w.nblk = (S + 127) / 128;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = o;
+    o = align_up(o + bytes, 1024);
+    return at;
+  };
+  w.q8 = take((size_t)H * w.SP * 128);
+  w.k8 = take((size_t)H * w.SP * 128);
+  w.vt8 = take((size_t)H * w.SP * 128);
+  w.qscale = take((size_t)H * w.SP * 4);
+  w.kscale = take((size_t)H * (w.SP / 128) * 4);
+  w.kmean = take((size_t)H * 128 * 4);
+  w.vscale = take((size_t)H * 128 * 4);
+  w.vinv = take((size_t)H * 128 * 4);
+  w.ksum = take((size_t)w.nblk * H * 128 * 4);
+  w.vmax = take((size_t)w.nblk * H * 128 * 4);
+  w.total = o;
+  return w;
+}
+
+}  // namespace
+
+extern "C" {
+
+int h3_version(void) { return H3B200_VERSION; }
+
+int h3_last_error(char* buf, int n) {
+  if (buf && n > 0) {
+    size_t k = g_err.size() < (size_t)(n - 1) ? g_err.size() : (size_t)(n - 1);
+    memcpy(buf, g_err.data(), k);
+    buf[k] = 0;
+  }
+  return (int)g_err.size();
+}
+
+int h3_device_status(int* status, int reset) {
+  if (!status) return fail(H3_ERR_ARG, "h3_device_status: status is NULL");
+  cudaError_t e = cudaMemcpyFromSymbol(status, g_status, sizeof(int));
+  if (e != cudaSuccess) return fail(H3_ERR_CUDA, "h3_device_status: %s", cudaGetErrorString(e));
+  if (reset) {
+    int zero = 0;
+    e = cudaMemcpyToSymbol(g_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return fail(H3_ERR_CUDA, "h3_device_status: %s", cudaGetErrorString(e));
+  }
+  return H3_OK;
+}
+
+size_t h3_sf_tiled_bytes(int rows, int cols) {
+  if (rows <= 0 || cols <= 0) return 0;
+  return (size_t)((rows + 127) / 128) * 128 * (size_t)(cols / 16);
+}
+
+// ------------------------------------------------------------------------------------------------ scales
+int h3_scales_begin(H3ScaleSlot* slots, int n, int delayed, int* clipped, void* stream) {
+  if (!slots || n <= 0) return fail(H3_ERR_ARG, "h3_scales_begin: slots NULL or n <= 0");
+  scales_begin_kernel<<<(n + 127) / 128, 128, 0, S_(stream)>>>(slots, n, delayed, clipped);
+  return check_launch("h3_scales_begin");
+}
+
+int h3_scales_dynamic(H3ScaleSlot* slot, void* stream) {
+  if (!slot) return fail(H3_ERR_ARG, "h3_scales_dynamic: slot is NULL");
+  act_from_amax_kernel<<<1, 1, 0, S_(stream)>>>(slot);
+  return check_launch("h3_scales_dynamic");
+}
+
+int h3_absmax_bf16(const void* x, long long ldx, int R, int K, float* out, void* stream) {
+  if (!x || !out) return fail(H3_ERR_ARG, "h3_absmax_bf16: NULL pointer");
+  if (R <= 0 || K <= 0 || K % 8 || ldx % 8 || !aligned(x, 16))
+    return fail(H3_ERR_SHAPE, "h3_absmax_bf16: need K %% 8 == 0, ldx %% 8 == 0, 16-byte aligned x");
+  long long n = (long long)R * (K / 8);
+  int blocks = (int)((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
+  absmax_kernel<<<blocks, 256, 0, S_(stream)>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, R, K, out);
+  return check_launch("h3_absmax_bf16");
+}
+
+// ------------------------------------------------------------------------------------------------ elementwise
+int h3_norm_mod(const void* x, int ldx, const float* w, const float* mod, const int* idx, int S, int D, int part,
+                float eps, void* out, int ldo, uint8_t* codes, uint8_t* sf, int sf_tiled, H3ScaleSlot* slot,
+                void* stream) {
+  if (!x || !w || !mod || !idx) return fail(H3_ERR_ARG, "h3_norm_mod: NULL input");
+  if (!out && !codes && !slot) return fail(H3_ERR_ARG, "h3_norm_mod: no output requested");
+  if (codes && (!sf || !slot)) return fail(H3_ERR_ARG, "h3_norm_mod: quantised output needs sf and slot");
+  if (part != 0 && part != 1) return fail(H3_ERR_ARG, "h3_norm_mod: part must be 0 or 1");
+  if (S <= 0 || D <= 0 || D % 16 || D > 6144 || ldx % 8 || (out && ldo % 8))
+    return fail(H3_ERR_SHAPE, "h3_norm_mod: need D %% 16 == 0, D <= 6144, row strides %% 8 == 0 (D=%d)", D);
+  if (!aligned(x, 16) || (out && !aligned(out, 16)) || (codes && !aligned(codes, 4)) || !aligned(w, 16) ||
+      !aligned(mod, 16))
+    return fail(H3_ERR_ARG, "h3_norm_mod: misaligned pointer");
+  NormModArgs a{reinterpret_cast<const __nv_bfloat16*>(x), ldx, w, mod, idx, S, D, part, eps,
+                reinterpret_cast<__nv_bfloat16*>(out), ldo, codes, sf, sf_tiled, slot};
+  const int rows_per_block = 8;
+  norm_mod_kernel<24><<<(S + rows_per_block - 1) / rows_per_block, 32 * rows_per_block, 0, S_(stream)>>>(a);
+  return check_launch("h3_norm_mod");
+}
+
+int h3_nvfp4_quant(const void* x, long long ldx, int cblk, long long blk_stride, int R, int K, const float* g_dev,
+                   float g, uint8_t* codes, uint8_t* sf, int sf_tiled, float* amax, void* stream) {
+  if (!x || !codes || !sf) return fail(H3_ERR_ARG, "h3_nvfp4_quant: NULL pointer");
+  if (R <= 0 || K <= 0 || K % 16 || cblk <= 0 || cblk % 16 || ldx % 8 || blk_stride % 8)
+    return fail(H3_ERR_SHAPE, "h3_nvfp4_quant: need K, cblk %% 16 == 0 and strides %% 8 == 0");
+  if (!g_dev && !(g > 0.f)) return fail(H3_ERR_ARG, "h3_nvfp4_quant: global scale must be > 0");
+  if (!aligned(x, 16) || !aligned(codes, 8)) return fail(H3_ERR_ARG, "h3_nvfp4_quant: misaligned pointer");
+  QuantArgs a{reinterpret_cast<const __nv_bfloat16*>(x), ldx, cblk, blk_stride, R, K, g_dev, g, codes, sf, sf_tiled,
+              amax};
+  long long n = (long long)R * (K / 16);
+  nvfp4_quant_kernel<<<(unsigned)((n + 255) / 256), 256, 0, S_(stream)>>>(a);
+  return check_launch("h3_nvfp4_quant");
+}
+
+int h3_gate_add(void* x, int ldx, const void* y, int ldy, const float* mod, const int* idx, int S, int D, int part,
+                void* stream) {
+  if (!x || !y || !mod || !idx) return fail(H3_ERR_ARG, "h3_gate_add: NULL pointer");
+  if (S <= 0 || D <= 0 || D % 8 || ldx % 8 || ldy % 8) return fail(H3_ERR_SHAPE, "h3_gate_add: need D %% 8 == 0");
+  if (part != 0 && part != 1) return fail(H3_ERR_ARG, "h3_gate_add: part must be 0 or 1");
+  long long n = (long long)S * (D / 8);
+  int blocks = (int)((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
+  gate_add_kernel<<<blocks, 256, 0, S_(stream)>>>(reinterpret_cast<__nv_bfloat16*>(x), ldx,
+                                                  reinterpret_cast<const __nv_bfloat16*>(y), ldy, mod, idx, S, D,
+                                                  part);
+  return check_launch("h3_gate_add");
+}
+
+int h3_act(const void* u, int ldu, void* out, int ldo, int M, int F, int act_kind, float* amax, void* stream) {
+  if (!u || !out) return fail(H3_ERR_ARG, "h3_act: NULL pointer");
+  if (M <= 0 || F <= 0 || F % 8 || ldu % 8 || ldo % 8) return fail(H3_ERR_SHAPE, "h3_act: need F %% 8 == 0");
+  if (act_kind != 0 && act_kind != 1) return fail(H3_ERR_ARG, "h3_act: act_kind must be 0 or 1");
+  long long n = (long long)M * (F / 8);
+  int blocks = (int)((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
+  act_kernel<<<blocks, 256, 0, S_(stream)>>>(reinterpret_cast<const __nv_bfloat16*>(u), ldu,
+                                             reinterpret_cast<__nv_bfloat16*>(out), ldo, M, F, act_kind, amax);
+  return check_launch("h3_act");
+}
+
+int h3_modulation(const float* t_emb, int M, int t_dim, const float* ada_w, const float* ada_b, int J, float* mod,
+                  void* stream) {
+  if (!t_emb || !ada_w || !ada_b || !mod) return fail(H3_ERR_ARG, "h3_modulation: NULL pointer");
+  if (M <= 0 || t_dim <= 0 || J <= 0) return fail(H3_ERR_SHAPE, "h3_modulation: bad sizes");
+  long long n = (long long)M * J;
+  modulation_kernel<<<(unsigned)((n + 255) / 256), 256, 0, S_(stream)>>>(t_emb, M, t_dim, ada_w, ada_b, J, mod);
+  return check_launch("h3_modulation");
+}
+
+// ------------------------------------------------------------------------------------------------ GEMM
+int h3_gemm_nvfp4(const uint8_t* a_codes, const uint8_t* a_sf, const H3ScaleSlot* a_slot, const uint8_t* b_codes,
+                  const uint8_t* b_sf, float g_b, const float* bias, int M, int N, int K, const H3Epilogue* epi,
+                  void* stream) {
+  if (!a_codes || !a_sf || !a_slot || !b_codes || !b_sf || !epi) return fail(H3_ERR_ARG, "h3_gemm_nvfp4: NULL pointer");
+  if (M <= 0 || N <= 0 || K <= 0 || K % 256 || N % 128)
+    return fail(H3_ERR_SHAPE, "h3_gemm_nvfp4: need K %% 256 == 0 and N %% 128 == 0 (M=%d N=%d K=%d)", M, N, K);
+  if (!aligned(a_codes, 16) || !aligned(b_codes, 16) || !aligned(a_sf, 16) || !aligned(b_sf, 16))
+    return fail(H3_ERR_ARG, "h3_gemm_nvfp4: codes and scales must be 16-byte aligned");
+  GemmArgs p{};
+  p.sfa = a_sf;
+  p.sfb = b_sf;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.a_slot = a_slot;
+  p.g_b = g_b;
+  p.bias = bias;
+  p.epi = epi->kind;
+  p.out = reinterpret_cast<__nv_bfloat16*>(epi->out);
+  p.ldo = epi->ldo;
+  p.x = reinterpret_cast<__nv_bfloat16*>(epi->x);
+  p.ldx = epi->ldx;
+  p.mod = epi->mod;
+  p.idx = epi->idx;
+  p.gate_part = epi->gate_part;
+  p.act_kind = epi->act_kind;
+  p.qcodes = epi->qcodes;
+  p.qsf = epi->qsf;
+  p.q_slot = epi->q_slot;
+  switch (epi->kind) {
+    case H3_EPI_STORE:
+      if (!p.out || p.ldo % 8 || !aligned(p.out, 16)) return fail(H3_ERR_ARG, "h3_gemm_nvfp4: STORE needs out");
+      break;
+    case H3_EPI_GATE_RESID:
+      if (!p.x || !p.mod || !p.idx || p.ldx % 8 || !aligned(p.x, 16) || (p.gate_part != 0 && p.gate_part != 1))
+        return fail(H3_ERR_ARG, "h3_gemm_nvfp4: GATE_RESID needs x, mod, idx, gate_part");
+      break;
+    case H3_EPI_ACT_BF16:
+    case H3_EPI_ACT_Q:
+      if (p.act_kind != 0 && p.act_kind != 1) return fail(H3_ERR_ARG, "h3_gemm_nvfp4: act_kind must be 0 or 1");
+      if (epi->kind == H3_EPI_ACT_BF16 && !p.out) return fail(H3_ERR_ARG, "h3_gemm_nvfp4: ACT_BF16 needs out");
+      if (epi->kind == H3_EPI_ACT_Q && (!p.qcodes || !p.qsf || !p.q_slot))
+        return fail(H3_ERR_ARG, "h3_gemm_nvfp4: ACT_Q needs qcodes, qsf, q_slot");
+      if (p.out && (p.ldo % 8 || !aligned(p.out, 16))) return fail(H3_ERR_ARG, "h3_gemm_nvfp4: misaligned out");
+      break;
+    default:
+      return fail(H3_ERR_ARG, "h3_gemm_nvfp4: unknown epilogue %d", epi->kind);
+  }
+  CUtensorMap ta, tb;
+  const int BN = (N % 256 == 0) ? 256 : 128;
+  int rc = make_map_u8(&ta, a_codes, K / 2, M, K / 2, 128, 128, "h3_gemm_nvfp4(A)");
+  if (rc) return rc;
+  rc = make_map_u8(&tb, b_codes, K / 2, N, K / 2, 128, BN, "h3_gemm_nvfp4(B)");
+  if (rc) return rc;
+  dim3 grid(N / BN, (M + 127) / 128);
+  if (BN == 256) {
+    rc = smem_optin(gemm_nvfp4_kernel<256>, GemmSmem<256>::TOTAL, &g_optin_gemm256, "h3_gemm_nvfp4");
+    if (rc) return rc;
+    gemm_nvfp4_kernel<256><<<grid, kGemmThreads, GemmSmem<256>::TOTAL, S_(stream)>>>(ta, tb, p);
+  } else {
+    rc = smem_optin(gemm_nvfp4_kernel<128>, GemmSmem<128>::TOTAL, &g_optin_gemm128, "h3_gemm_nvfp4");
+    if (rc) return rc;
+    gemm_nvfp4_kernel<128><<<grid, kGemmThreads, GemmSmem<128>::TOTAL, S_(stream)>>>(ta, tb, p);
+  }
+  return check_launch("h3_gemm_nvfp4");
+}
+
+// ------------------------------------------------------------------------------------------------ attention
+int h3_qknorm_rope(void* q, void* k, long long ld, int S, int H, int rot, const float* qw, const float* kw,
+                   const float* rope, float eps, void* stream) {
+  if (!q || !k || !qw || !kw || (rot > 0 && !rope)) return fail(H3_ERR_ARG, "h3_qknorm_rope: NULL pointer");
+  if (S <= 0 || H <= 0 || rot < 0 || rot > 128 || rot % 8 || ld % 4)
+    return fail(H3_ERR_SHAPE, "h3_qknorm_rope: need rot %% 8 == 0, rot <= 128, ld %% 4 == 0");
+  if (!aligned(q, 8) || !aligned(k, 8) || (rope && !aligned(rope, 16)))
+    return fail(H3_ERR_ARG, "h3_qknorm_rope: misaligned pointer");
+  QkNormArgs a{reinterpret_cast<__nv_bfloat16*>(q), reinterpret_cast<__nv_bfloat16*>(k), ld, S, H, rot, qw, kw, rope,
+               eps};
+  long long rows = (long long)S * 2 * H;
+  qknorm_rope_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, S_(stream)>>>(a);
+  return check_launch("h3_qknorm_rope");
+}
+
+size_t h3_attn_workspace_bytes(int S, int H) {
+  if (S <= 0 || H <= 0) return 0;
+  return attn_ws(S, H).total;
+}
+
+int h3_attn_fp8(const void* q, const void* k, const void* v, long long ld, long long hstride, int S, int H, void* out,
+                long long ldo, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!q || !k || !v || !out || !workspace) return fail(H3_ERR_ARG, "h3_attn_fp8: NULL pointer");
+  if (S <= 0 || H <= 0 || ld % 8 || hstride % 8 || ldo % 8)
+    return fail(H3_ERR_SHAPE, "h3_attn_fp8: need strides %% 8 == 0");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16) || !aligned(workspace, 1024))
+    return fail(H3_ERR_ARG, "h3_attn_fp8: q/k/v/out 16-byte and workspace 1024-byte alignment required");
+  AttnWs w = attn_ws(S, H);
+  if (workspace_bytes < w.total)
+    return fail(H3_ERR_ARG, "h3_attn_fp8: workspace %zu bytes < %zu", workspace_bytes, w.total);
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  uint8_t* q8 = ws + w.q8;
+  uint8_t* k8 = ws + w.k8;
+  uint8_t* vt8 = ws + w.vt8;
+  float* qscale = reinterpret_cast<float*>(ws + w.qscale);
+  float* kscale = reinterpret_cast<float*>(ws + w.kscale);
+  float* kmean = reinterpret_cast<float*>(ws + w.kmean);
+  float* vscale = reinterpret_cast<float*>(ws + w.vscale);
+  float* vinv = reinterpret_cast<float*>(ws + w.vinv);
+  float* ksum = reinterpret_cast<float*>(ws + w.ksum);
+  float* vmax = reinterpret_cast<float*>(ws + w.vmax);
+  AttnView view{reinterpret_cast<const __nv_bfloat16*>(q), reinterpret_cast<const __nv_bfloat16*>(k),
+                reinterpret_cast<const __nv_bfloat16*>(v), ld, hstride};
+  cudaStream_t st = S_(stream);
+  attn_stats_kernel<<<dim3(w.nblk, H), 128, 0, st>>>(view, S, H, ksum, vmax);
+  int rc = check_launch("h3_attn_fp8(stats)");
+  if (rc) return rc;
+  attn_stats_reduce_kernel<<<(H * 128 + 127) / 128, 128, 0, st>>>(ksum, vmax, w.nblk, S, H, kmean, vscale, vinv);
+  if ((rc = check_launch("h3_attn_fp8(reduce)"))) return rc;
+  attn_quant_kernel<<<dim3(w.SP / 128, H), 128, 0, st>>>(view, S, w.SP, H, kmean, vinv, q8, qscale, k8, kscale, vt8);
+  if ((rc = check_launch("h3_attn_fp8(quant)"))) return rc;
+  CUtensorMap tq, tk, tv;
+  if ((rc = make_map_u8(&tq, q8, 128, (uint64_t)H * w.SP, 128, 128, 128, "h3_attn_fp8(Q)"))) return rc;
+  if ((rc = make_map_u8(&tk, k8, 128, (uint64_t)H * w.SP, 128, 128, 128, "h3_attn_fp8(K)"))) return rc;
+  if ((rc = make_map_u8(&tv, vt8, w.SP, (uint64_t)H * 128, w.SP, 128, 128, "h3_attn_fp8(V)"))) return rc;
+  if ((rc = smem_optin(attn_fp8_kernel, AttnSmem::TOTAL, &g_optin_attn, "h3_attn_fp8"))) return rc;
+  AttnArgs p{qscale, kscale, vscale, reinterpret_cast<__nv_bfloat16*>(out), ldo, S, w.SP, H};
+  attn_fp8_kernel<<<dim3(w.SP / 256, H), kAttnThreads, AttnSmem::TOTAL, st>>>(tq, tk, tv, p);
+  return check_launch("h3_attn_fp8");
+}
+
+}  // extern "C"
