@@ -191,6 +191,65 @@ def reference_arm(a) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------------------------ single ops
+def micro(a) -> None:
+    """One op alone on synthetic inputs, timed with CUDA events (kernel-level numbers and ncu targets)."""
+
+    from tfvideo import attention as A
+    from tfvideo import linear as L
+    from tfvideo import native as N
+
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    if a.micro == "attn":
+        S, H = a.seq, a.heads
+        qkv = torch.randn(S, 3 * H * 128, generator=g, device="cuda").to(torch.bfloat16)
+        out = torch.empty(S, H * 128, dtype=torch.bfloat16, device="cuda")
+        ws = torch.empty(N.attn_workspace_bytes(S, H) + 1024, dtype=torch.uint8, device="cuda")
+        HD = H * 128
+
+        def run():
+            A.fp8_tokens(qkv[:, :HD], qkv[:, HD:2 * HD], qkv[:, 2 * HD:], S, H, 3 * HD, 128, out, ws)
+        flops = 4.0 * S * S * H * 128
+        what = f"attn S={S} H={H}"
+    else:
+        M, Nn, K = (int(v) for v in a.mnk.split(","))
+        w = (torch.randn(Nn, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        lin = L.Nvfp4Linear(w)
+        x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+        lin.set_act(float(x.float().abs().amax()) / 2688)
+        codes, sf = L.quantize(x, g_ptr=lin.slot_ptr() + 4)
+        out = torch.empty(M, Nn, dtype=torch.bfloat16, device="cuda")
+        mod = torch.randn(4, 6, Nn, generator=g, device="cuda") * 0.1
+        idx = torch.zeros(M, dtype=torch.int32, device="cuda")
+        qs = L.new_slots(1, "cuda")
+        qs[0, 1] = 1.0
+        qc = torch.empty(M, Nn // 2, dtype=torch.uint8, device="cuda")
+        qsf = torch.zeros(N.sf_tiled_bytes(M, Nn), dtype=torch.uint8, device="cuda")
+        epi = {"store": N.H3Epilogue(kind=N.H3_EPI_STORE, out=out.data_ptr(), ldo=Nn),
+               "gate": N.H3Epilogue(kind=N.H3_EPI_GATE_RESID, x=out.data_ptr(), ldx=Nn, mod=mod.data_ptr(),
+                                    idx=idx.data_ptr(), gate_part=0),
+               "act_q": N.H3Epilogue(kind=N.H3_EPI_ACT_Q, act_kind=N.ACT_GELU, qcodes=qc.data_ptr(),
+                                     qsf=qsf.data_ptr(), q_slot=N.slot_ptr(qs, 0))}[a.epi]
+
+        def run():
+            lin.gemm(codes, sf, M, epi)
+        flops = 2.0 * M * Nn * K
+        what = f"gemm M={M} N={Nn} K={K} epi={a.epi}"
+    for _ in range(a.warmup):
+        run()
+    torch.cuda.synchronize()
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record()
+    for _ in range(a.steps):
+        run()
+    en.record()
+    torch.cuda.synchronize()
+    ms = st.elapsed_time(en) / a.steps
+    print(json.dumps({"micro": what, "ms": ms, "tflops": flops / ms / 1e9, "device_status": N.device_status()}),
+          flush=True)
+
+
 # ------------------------------------------------------------------------------------------------ GPU leg
 def main():
     ap = argparse.ArgumentParser()
@@ -203,9 +262,15 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=512)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--micro", choices=["attn", "gemm"], help="time one op alone (BASELINE configs 1 / 2)")
+    ap.add_argument("--heads", type=int, default=40)
+    ap.add_argument("--mnk", default="37760,15360,5120", help="--micro gemm: M,N,K")
+    ap.add_argument("--epi", default="store", choices=["store", "gate", "act_q"])
     a = ap.parse_args()
     if a.impl == "reference":
         return reference_arm(a)
+    if a.micro:
+        return micro(a)
 
     from tfvideo import minimax_h3 as M
     from tfvideo import native as N

@@ -11,6 +11,8 @@
 // row's max grows by more than tau).
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 #include "h3b200.h"
 
@@ -240,6 +242,46 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float m;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
+  return m;
+}
+// (exp2(a * scale - bias), exp2(b * scale - bias)) as f16x2 (a in the low half): one packed fp32 FMA, one packed
+// conversion and one MUFU ex2 for two probabilities.  P is rounded to e4m3 next, so f16 precision is ample.
+__device__ __forceinline__ uint32_t exp2_pair(float a, float b, uint64_t scale2, uint64_t nbias2) {
+  uint32_t h;
+  asm("{\n\t.reg .b64 x, y;\n\t.reg .f32 y0, y1;\n\t.reg .b32 hh;\n\t"
+      "mov.b64 x, {%1, %2};\n\t"
+      "fma.rn.f32x2 y, x, %3, %4;\n\t"
+      "mov.b64 {y0, y1}, y;\n\t"
+      "cvt.rn.f16x2.f32 hh, y1, y0;\n\t"
+      "ex2.approx.f16x2 %0, hh;\n\t}"
+      : "=r"(h)
+      : "f"(a), "f"(b), "l"(scale2), "l"(nbias2));
+  return h;
+}
+__device__ __forceinline__ uint64_t f32x2_splat(float v) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(v));
+  return r;
+}
+__device__ __forceinline__ uint32_t hadd2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ float hsum2_f32(uint32_t h) {
+  __half2 v = *reinterpret_cast<__half2*>(&h);
+  return __low2float(v) + __high2float(v);
+}
+// two f16x2 pairs -> four e4m3 bytes (lo pair's low half in byte 0)
+__device__ __forceinline__ uint32_t e4m3x4_f16(uint32_t lo, uint32_t hi) {
+  uint16_t a, b;
+  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(a) : "r"(lo));
+  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(b) : "r"(hi));
+  return (uint32_t)a | ((uint32_t)b << 16);
+}
 
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_fp8_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -380,16 +422,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tmem_ld_wait();
       const float scale = qr * ksc[j];
       const int valid = p.S - j * 128;   // keys of this tile inside the sequence
-      float mx = -INFINITY;
+      if (valid < 128) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          float s = __uint_as_float(sr[c][e]);
-          if (c * 32 + e >= valid) s = -INFINITY;
-          sr[c][e] = __float_as_uint(s);
-          mx = fmaxf(mx, s);
-        }
+          for (int e = 0; e < 32; ++e)
+            if (c * 32 + e >= valid) sr[c][e] = __float_as_uint(-INFINITY);
+      }
+      float m4[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float m = __uint_as_float(sr[c][0]);
+#pragma unroll
+        for (int e = 1; e < 31; e += 2) m = max3(m, __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
+        m4[c] = fmaxf(m, __uint_as_float(sr[c][31]));
+      }
+      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       const float mnew = mx * scale;
       // raise the running max only when a row's max grew by more than tau; the tcgen05 ld/st of O are warp-wide,
       // so a warp rescales when any of its rows must (the others multiply by 1)
@@ -412,20 +460,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         l *= alpha;
         m_used = mnew;
       }
-      const float bias = m_used - kPOffset;
+      const uint64_t scale2 = f32x2_splat(scale), nbias2 = f32x2_splat(kPOffset - m_used);
       float lsum = 0.f;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pw[8];
+        uint32_t hs = 0;
 #pragma unroll
         for (int w = 0; w < 8; ++w) {
-          float e0 = ex2(fmaf(__uint_as_float(sr[c][4 * w + 0]), scale, -bias));
-          float e1 = ex2(fmaf(__uint_as_float(sr[c][4 * w + 1]), scale, -bias));
-          float e2 = ex2(fmaf(__uint_as_float(sr[c][4 * w + 2]), scale, -bias));
-          float e3 = ex2(fmaf(__uint_as_float(sr[c][4 * w + 3]), scale, -bias));
-          lsum += (e0 + e1) + (e2 + e3);
-          pw[w] = e4m3x2(e0, e1) | (e4m3x2(e2, e3) << 16);
+          const uint32_t e0 = exp2_pair(__uint_as_float(sr[c][4 * w]), __uint_as_float(sr[c][4 * w + 1]), scale2,
+                                        nbias2);
+          const uint32_t e1 = exp2_pair(__uint_as_float(sr[c][4 * w + 2]), __uint_as_float(sr[c][4 * w + 3]), scale2,
+                                        nbias2);
+          hs = hadd2(hs, hadd2(e0, e1));
+          pw[w] = e4m3x4_f16(e0, e1);
         }
+        lsum += hsum2_f32(hs);
         tmem_st8(s_col + c * 8, pw);
       }
       l += lsum;

@@ -257,9 +257,10 @@ __global__ void __launch_bounds__(256) gate_add_kernel(__nv_bfloat16* x, int ldx
 
 // ------------------------------------------------------------------------------------------------ activations
 __device__ __forceinline__ float gelu_tanh_f(float u) {
-  // 0.5 u (1 + tanh(sqrt(2/pi) (u + 0.044715 u^3)))
-  float t = tanhf(0.7978845608028654f * (u + 0.044715f * u * u * u));
-  return 0.5f * u * (1.0f + t);
+  // 0.5 u (1 + tanh(z)) with z = sqrt(2/pi) (u + 0.044715 u^3), evaluated as u * sigmoid(2 z) = u / (1 + e^(-2z)):
+  // the same function without the cancellation of 1 + tanh(z) for negative z
+  const float z2 = 1.5957691216057308f * (u + 0.044715f * u * u * u);
+  return __fdividef(u, 1.0f + __expf(-z2));
 }
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
 

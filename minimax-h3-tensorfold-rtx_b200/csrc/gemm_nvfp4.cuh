@@ -143,14 +143,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;
     const int row = m0 + q * 32 + lane;
+    const bool live = row < p.M;
+    __nv_bfloat16* __restrict__ xrow = nullptr;
+    const float* __restrict__ gate = nullptr;
+    if (p.epi == H3_EPI_GATE_RESID && live) {
+      // the residual tile is read after the mainloop: pull this row's 2 * BN bytes into L2 while the MMAs run
+      xrow = p.x + (size_t)row * p.ldx + n0;
+      gate = p.mod + ((size_t)p.idx[row] * 6 + 3 * p.gate_part + 2) * p.N + n0;
+#pragma unroll
+      for (int b = 0; b < BN * 2; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"((const char*)xrow + b));
+    }
     const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, 103));   // tcgen05.ld below is warp-wide
     tc_fence_after();
     if (ok) {
       const float alpha = p.a_slot->act * p.g_b;
-      const bool live = row < p.M;
-      const float* gate = nullptr;
-      if (p.epi == H3_EPI_GATE_RESID && live)
-        gate = p.mod + ((size_t)p.idx[row] * 6 + 3 * p.gate_part + 2) * p.N;
       float inv_q = 0.f;
       if (p.epi == H3_EPI_ACT_Q) inv_q = __fdiv_rn(1.0f, p.q_slot->act);
       float amax = 0.f;
@@ -158,6 +164,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
+        // issue this chunk's global loads (residual, gate) before the TMEM load so their latency overlaps it
+        uint4 xu[4];
+        float4 ga[8];
+        if (xrow) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) xu[j] = reinterpret_cast<const uint4*>(xrow + c * 32)[j];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ga[j] = reinterpret_cast<const float4*>(gate + c * 32)[j];
+        }
         __syncwarp();
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, r);
         tmem_ld_wait();
@@ -176,23 +191,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             o[j] = make_uint4(pack_bf16(v[8 * j], v[8 * j + 1]), pack_bf16(v[8 * j + 2], v[8 * j + 3]),
                               pack_bf16(v[8 * j + 4], v[8 * j + 5]), pack_bf16(v[8 * j + 6], v[8 * j + 7]));
         } else if (p.epi == H3_EPI_GATE_RESID) {
-          uint4* xp = reinterpret_cast<uint4*>(p.x + (size_t)row * p.ldx + nc);
+          const float* g = reinterpret_cast<const float*>(ga);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            uint4 xu = xp[j];
-            uint32_t* xw = &xu.x;
-            float4 g0 = *reinterpret_cast<const float4*>(gate + nc + 8 * j);
-            float4 g1 = *reinterpret_cast<const float4*>(gate + nc + 8 * j + 4);
-            const float ga[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+            uint32_t* xw = &xu[j].x;
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              float y0 = bf16_round(v[8 * j + 2 * e]), y1 = bf16_round(v[8 * j + 2 * e + 1]);
-              float lo = __fadd_rn(bf16_lo(xw[e]), __fmul_rn(y0, ga[2 * e]));
-              float hi = __fadd_rn(bf16_hi(xw[e]), __fmul_rn(y1, ga[2 * e + 1]));
+              const int k = 8 * j + 2 * e;
+              float lo = __fadd_rn(bf16_lo(xw[e]), __fmul_rn(bf16_round(v[k]), g[k]));
+              float hi = __fadd_rn(bf16_hi(xw[e]), __fmul_rn(bf16_round(v[k + 1]), g[k + 1]));
               xw[e] = pack_bf16(lo, hi);
             }
-            xp[j] = xu;
           }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(xrow + c * 32)[j] = xu[j];
         } else {
           // activation: gelu -> 32 outputs at columns nc.., swiglu -> 16 outputs at columns nc / 2..
           float a[32];

@@ -90,22 +90,38 @@ def gelu_tanh(u) -> np.ndarray:
 
 
 # ------------------------------------------------------------------------------------------ qk norm + rope
+def _head_sumsq_lanes(x: np.ndarray) -> np.ndarray:
+    """Sum of squares over the last dim (128) in the CUDA kernel's order: lane l owns dims 4l..4l+3, accumulated in
+    order as rounded fp32 products and sums, then combined by an xor butterfly (16, 8, 4, 2, 1)."""
+
+    lanes = np.arange(32)
+    v = x.reshape(*x.shape[:-1], 32, 4)
+    acc = np.zeros(v.shape[:-1], dtype=np.float32)
+    for e in range(4):
+        acc = (acc + (v[..., e] * v[..., e]).astype(np.float32)).astype(np.float32)
+    for k in (16, 8, 4, 2, 1):
+        acc = (acc + acc[..., lanes ^ k]).astype(np.float32)
+    return acc[..., 0]
+
+
 def qknorm_rope(x, w, rope, eps: float) -> np.ndarray:
-    """Per-head RMSNorm with weight w [Dh], then split-half RoPE over the first rot_dim dims, bf16 out.
+    """Per-head RMSNorm with weight w [Dh = 128], then split-half RoPE over the first rot_dim dims, bf16 out.
 
     Restates the call ``ck.rms_rope_split_half_(q, k, rope_freqs, q_norm, k_norm, epsilon, rot_dim)``
-    (tfvideo/minimax_h3.py:296-298): x [S, H, Dh]; rope [S, rot/2, 2, 2] holds one 2x2 rotation per (token, pair)
+    (tfvideo/minimax_h3.py:296-298): x [S, H, 128]; rope [S, rot/2, 2, 2] holds one 2x2 rotation per (token, pair)
     as built in tools/profile_block.py:41-45 (``[[cos, -sin], [sin, cos]]``).  Pair i couples dims i and
     i + rot/2:  o_i = f00 * y_i + f01 * y_{i+half},  o_{i+half} = f10 * y_i + f11 * y_{i+half}.  Dims at and past
-    rot_dim only get the norm.  fp32 inside, one bf16 rounding at the end (comfy-kitchen's own rounding is not in
-    the reference tree; this is the convention the CUDA kernel follows)."""
+    rot_dim only get the norm.  fp32 inside (the sum of squares in the lane order of ``_head_sumsq_lanes``, an IEEE
+    sqrt and division, rounded products and sums), one bf16 rounding at the end -- comfy-kitchen's own rounding is
+    not in the reference tree; this is the convention the CUDA kernel follows bit for bit."""
 
     x = f32(x)
     S, H, Dh = x.shape
     rope = f32(rope)
     half = rope.shape[1]
-    ss = (x.astype(np.float64) ** 2).sum(-1)
-    r = (1.0 / np.sqrt(ss / Dh + eps)).astype(np.float32)
+    ss = _head_sumsq_lanes(x)
+    var = ((ss / F32(Dh)).astype(np.float32) + F32(eps)).astype(np.float32)
+    r = (F32(1.0) / np.sqrt(var)).astype(np.float32)
     y = (x * r[..., None]).astype(np.float32)
     y = (y * f32(w)[None, None, :]).astype(np.float32)
     out = y.copy()

@@ -1,0 +1,134 @@
+"""Ulysses sequence parallelism (tfvideo/parallel.py) on CPU ranks over gloo, world size 2 and 4.
+
+The same SequenceParallel code the engine runs over NCCL: tokens sharded over ranks, one all-to-all per q / k / v to
+head-parallel layout, attention per rank on its heads over the full sequence, one all-to-all back.  Checked against
+the unsharded computation; plus the failure paths: a rank that never joins ends the others' collective with an
+error, within the process group's timeout.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import sys
+import traceback
+from datetime import timedelta
+from pathlib import Path
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _init(rank, world, port, timeout=30):
+    sys.path.insert(0, str(ROOT / "minimax-h3-tensorfold-rtx_b200"))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=timeout))
+
+
+def _ulysses_worker(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        from tfvideo.parallel import SequenceParallel, unshard_columns
+
+        sp = SequenceParallel()
+        S, H, Dh = 48, 8, 16
+        g = torch.Generator().manual_seed(0)
+        qkv = torch.randn(S, 3, H, Dh, generator=g)
+        t0, n = sp.shard(S)
+        local = qkv[t0:t0 + n]
+        outs = []
+        for j in range(3):
+            buf = torch.empty(S, H // world, Dh)
+            sp.heads_from_tokens(local[:, j], buf)
+            ref = qkv[:, j, rank * (H // world):(rank + 1) * (H // world)]
+            assert torch.equal(buf, ref), f"rank {rank}: head gather mismatch for tensor {j}"
+            outs.append(buf)
+        # attention on this rank's heads over the full sequence, then back to token-sharded rows
+        qh, kh, vh = (t.transpose(0, 1) for t in outs)
+        o = torch.nn.functional.scaled_dot_product_attention(qh, kh, vh).transpose(0, 1).reshape(S, -1)
+        recv = torch.empty(world, n, (H // world) * Dh)
+        sp.tokens_from_heads(o.contiguous(), recv)
+        got = unshard_columns(recv)
+        full = torch.nn.functional.scaled_dot_product_attention(*(qkv[:, j].transpose(0, 1) for j in range(3)))
+        want = full.transpose(0, 1).reshape(S, H * Dh)[t0:t0 + n]
+        assert torch.allclose(got, want, atol=1e-5), f"rank {rank}: attention through Ulysses differs"
+        m = torch.tensor([float(rank + 1)])
+        sp.max_(m)
+        assert m.item() == world
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception:  # noqa: BLE001
+        q.put((rank, traceback.format_exc()))
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_ulysses_matches_unsharded(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_ulysses_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in ps)
+    for p in ps:
+        p.join(30)
+    assert all(v == "ok" for v in res.values()), res
+
+
+def _straggler_worker(rank, world, port, q):
+    """Rank 1 joins the group but never enters the all-to-all: rank 0's collective must fail, not hang."""
+
+    try:
+        _init(rank, world, port, timeout=5)
+        from tfvideo.parallel import SequenceParallel
+
+        sp = SequenceParallel()
+        if rank == 1:
+            q.put((rank, "skipped"))
+            import time
+            time.sleep(15)
+            return
+        buf = torch.empty(8, 2, 4)
+        try:
+            sp.heads_from_tokens(torch.randn(4, 4, 4), buf)
+            q.put((rank, "no error"))
+        except Exception as e:  # noqa: BLE001
+            q.put((rank, f"error: {type(e).__name__}"))
+    except Exception:  # noqa: BLE001
+        q.put((rank, traceback.format_exc()))
+
+
+def test_missing_rank_fails_collective():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_straggler_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in ps)
+    for p in ps:
+        p.join(30)
+        if p.is_alive():
+            p.kill()
+    assert res[1] == "skipped"
+    assert res[0].startswith("error"), res
+
+
+def test_shard_requires_even_split():
+    from tfvideo.parallel import SequenceParallel
+
+    sp = SequenceParallel.__new__(SequenceParallel)
+    sp.world, sp.rank, sp.group = 8, 3, None
+    assert sp.shard(37760) == (3 * 4720, 4720)
+    with pytest.raises(ValueError):
+        sp.shard(37790)

@@ -170,5 +170,5 @@ def test_gate_add_and_activations():
     assert np.abs(sw - OO.swiglu(gu)).max() <= 2 ** -7 * np.abs(OO.swiglu(gu)).max()
     ge = to_np(K.gelu_tanh(to_dev(gu)))
     ref = OO.gelu_tanh(gu)
-    ulps = np.abs(ge.view(np.int32).astype(np.int64) - ref.view(np.int32).astype(np.int64)) >> 16
-    assert ulps.max() <= 1
+    assert (np.abs(ge - ref) <= 2.0 ** -7 * np.abs(ref) + 1e-30).all()     # relative, also in the far negative tail
+    assert (ge == ref).mean() > 0.95
