@@ -233,7 +233,9 @@ struct AttnSmem {
   static constexpr int TILE = 128 * 128;
   static constexpr int Q_OFF = 0;                       // Q0, Q1
   static constexpr int KV_OFF = 2 * TILE;               // per stage: K, V^T
-  static constexpr int BAR_OFF = KV_OFF + kAttnStages * 2 * TILE;
+  static constexpr int KSC_OFF = KV_OFF + kAttnStages * 2 * TILE;   // this head's K-block scales
+  static constexpr int MAX_KBLK = 2048;                                // sequences up to 262,144 tokens
+  static constexpr int BAR_OFF = KSC_OFF + MAX_KBLK * 4;
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;
 };
 
@@ -303,6 +305,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int h = blockIdx.y;
   const int q0 = blockIdx.x * 256;
   const int nkv = (p.S + 127) / 128;
+  float* ksc_s = reinterpret_cast<float*>(smem + L::KSC_OFF);
+  for (int i = threadIdx.x; i < nkv; i += blockDim.x) ksc_s[i] = p.kscale[(size_t)h * (p.SP / 128) + i];
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -408,7 +412,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t s_col = tmem + lane_off + i * 128;
     const uint32_t o_col = tmem + lane_off + 256 + i * 128;
     const float qr = p.qscale[(size_t)h * p.SP + query];
-    const float* ksc = p.kscale + (size_t)h * (p.SP / 128);
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
@@ -416,28 +419,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      uint32_t sr[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(s_col + c * 32, sr[c]);
-      tmem_ld_wait();
-      const float scale = qr * ksc[j];
+      const float scale = qr * ksc_s[j];
       const int valid = p.S - j * 128;   // keys of this tile inside the sequence
-      if (valid < 128) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (c * 32 + e >= valid) sr[c][e] = __float_as_uint(-INFINITY);
-      }
-      float m4[4];
+      // pass 1: the row max of the raw scores (keys past S masked in the last tile)
+      float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        float m = __uint_as_float(sr[c][0]);
+        uint32_t sr[32];
+        tmem_ld32(s_col + c * 32, sr);
+        tmem_ld_wait();
+        if (valid < 128) {
 #pragma unroll
-        for (int e = 1; e < 31; e += 2) m = max3(m, __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
-        m4[c] = fmaxf(m, __uint_as_float(sr[c][31]));
+          for (int e = 0; e < 32; ++e)
+            if (c * 32 + e >= valid) sr[e] = __float_as_uint(-INFINITY);
+        }
+        float m = __uint_as_float(sr[0]);
+#pragma unroll
+        for (int e = 1; e < 31; e += 2) m = max3(m, __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]));
+        mx = max3(mx, m, __uint_as_float(sr[31]));
       }
-      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       const float mnew = mx * scale;
       // raise the running max only when a row's max grew by more than tau; the tcgen05 ld/st of O are warp-wide,
       // so a warp rescales when any of its rows must (the others multiply by 1)
@@ -462,15 +462,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       const uint64_t scale2 = f32x2_splat(scale), nbias2 = f32x2_splat(kPOffset - m_used);
       float lsum = 0.f;
+      // pass 2: P = exp2(s * scale - m + c) -> e4m3, written over the first 32 columns of S (read chunk c before
+      // writing chunk c's P words, which land in columns the earlier chunks already consumed)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
+        uint32_t sr[32];
+        tmem_ld32(s_col + c * 32, sr);
+        tmem_ld_wait();
+        if (valid < 128) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (c * 32 + e >= valid) sr[e] = __float_as_uint(-INFINITY);
+        }
         uint32_t pw[8];
         uint32_t hs = 0;
 #pragma unroll
         for (int w = 0; w < 8; ++w) {
-          const uint32_t e0 = exp2_pair(__uint_as_float(sr[c][4 * w]), __uint_as_float(sr[c][4 * w + 1]), scale2,
-                                        nbias2);
-          const uint32_t e1 = exp2_pair(__uint_as_float(sr[c][4 * w + 2]), __uint_as_float(sr[c][4 * w + 3]), scale2,
+          const uint32_t e0 = exp2_pair(__uint_as_float(sr[4 * w]), __uint_as_float(sr[4 * w + 1]), scale2, nbias2);
+          const uint32_t e1 = exp2_pair(__uint_as_float(sr[4 * w + 2]), __uint_as_float(sr[4 * w + 3]), scale2,
                                         nbias2);
           hs = hadd2(hs, hadd2(e0, e1));
           pw[w] = e4m3x4_f16(e0, e1);

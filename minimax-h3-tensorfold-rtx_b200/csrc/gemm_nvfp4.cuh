@@ -48,10 +48,14 @@ struct GemmSmem {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
   static constexpr int BAR_OFF = kGemmStages * STAGE_BYTES;
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;     // barriers + TMEM address word + alignment slack
-  // TMEM columns: accumulator [0, BN), A scales (4 per MMA K step, 4 steps), B scales (BN / 32 per K step, 4 steps)
+  // TMEM columns: accumulator [0, BN), then one scale-factor buffer per smem stage: A scales (4 columns per MMA K
+  // step, 4 steps) and B scales (BN / 32 per K step).  A K-tile's copies go to its own buffer, so they never wait for
+  // the previous K-tile's MMAs to finish reading theirs.
+  static constexpr int SF_COLS = 16 + BN / 8;
   static constexpr int SFA_COL = BN;
   static constexpr int SFB_COL = BN + 16;
   static constexpr int TMEM_COLS = 512;
+  static_assert(BN + kGemmStages * SF_COLS <= TMEM_COLS, "TMEM budget");
 };
 
 __device__ __forceinline__ float act_apply(int kind, float g, float u) {
@@ -123,17 +127,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t a_s = smem_u32(st), b_s = smem_u32(st + L::A_BYTES);
         const uint32_t sfa_s = smem_u32(st + L::A_BYTES + L::B_BYTES);
         const uint32_t sfb_s = sfa_s + L::SFA_BYTES;
+        const uint32_t sf_t = tmem + s * L::SF_COLS;   // this stage's scale-factor buffer
 #pragma unroll
         for (int kb = 0; kb < 4; ++kb) {
-          tmem_cp_32x128b_x4(tmem + L::SFA_COL + 4 * kb, sdesc_sf_atom(sfa_s + kb * 512));
+          tmem_cp_32x128b_x4(sf_t + L::SFA_COL + 4 * kb, sdesc_sf_atom(sfa_s + kb * 512));
 #pragma unroll
           for (int nb = 0; nb < BN / 128; ++nb)
-            tmem_cp_32x128b_x4(tmem + L::SFB_COL + (BN / 32) * kb + 4 * nb, sdesc_sf_atom(sfb_s + nb * 2048 + kb * 512));
+            tmem_cp_32x128b_x4(sf_t + L::SFB_COL + (BN / 32) * kb + 4 * nb, sdesc_sf_atom(sfb_s + nb * 2048 + kb * 512));
         }
 #pragma unroll
         for (int kb = 0; kb < 4; ++kb) {
           mma_nvfp4(tmem, sdesc_kmajor_sw128(a_s + kb * 32), sdesc_kmajor_sw128(b_s + kb * 32), idesc,
-                    tmem + L::SFA_COL + 4 * kb, tmem + L::SFB_COL + (BN / 32) * kb, (kt | kb) != 0);
+                    sf_t + L::SFA_COL + 4 * kb, sf_t + L::SFB_COL + (BN / 32) * kb, (kt | kb) != 0);
         }
         tc_commit(&empty[s]);
       }

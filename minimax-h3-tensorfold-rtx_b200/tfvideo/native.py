@@ -14,7 +14,7 @@ from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().parent / "_native" / "libh3b200.so"
+LIB_PATH = Path(os.environ.get("H3B200_LIB") or Path(__file__).resolve().parent / "_native" / "libh3b200.so")
 
 H3_EPI_STORE, H3_EPI_GATE_RESID, H3_EPI_ACT_BF16, H3_EPI_ACT_Q = 0, 1, 2, 3
 ACT_GELU, ACT_SWIGLU = 0, 1

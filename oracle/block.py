@@ -121,7 +121,8 @@ def rope_table(S: int, rot_dim: int = 128, splits=(44, 42, 42), grid=None, theta
     ``grid`` defaults to the smallest cube-ish grid covering S."""
 
     half = rot_dim // 2
-    parts = [s // 2 for s in splits]
+    tot = sum(splits)
+    parts = [int(round(s * half / tot)) for s in splits]
     parts[-1] = half - sum(parts[:-1])
     if grid is None:
         w = max(1, int(round(S ** (1 / 3))))

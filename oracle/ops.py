@@ -82,11 +82,15 @@ def swiglu(gu, rnd=bf16_round) -> np.ndarray:
 
 
 def gelu_tanh(u) -> np.ndarray:
-    """GELU with the tanh approximation, bf16 out; BASELINE's FFN activation (torch's gelu(approximate="tanh"))."""
+    """GELU with the tanh approximation, bf16 out; BASELINE's FFN activation (torch's gelu(approximate="tanh")).
+
+    0.5 u (1 + tanh(z)) with z = sqrt(2/pi) (u + 0.044715 u^3), evaluated in float64 as u / (1 + exp(-2 z)) -- the
+    same function, without the cancellation of 1 + tanh(z) that flushes the far negative tail to zero."""
 
     u = f32(u).astype(np.float64)
-    c = math.sqrt(2.0 / math.pi)
-    return bf16_round((0.5 * u * (1.0 + np.tanh(c * (u + 0.044715 * u ** 3)))).astype(np.float32))
+    z = math.sqrt(2.0 / math.pi) * (u + 0.044715 * u ** 3)
+    with np.errstate(over="ignore"):
+        return bf16_round((u / (1.0 + np.exp(-2.0 * z))).astype(np.float32))
 
 
 # ------------------------------------------------------------------------------------------ qk norm + rope

@@ -103,7 +103,7 @@ def test_gemm_gate_residual(part):
     # y may differ from the reference by one bf16 ulp where the fp64 result sits near a rounding boundary; that
     # moves x + y * gate by at most |gate| * ulp(y) before x's own rounding
     g = mod[idx, 3 * part + 2]
-    bound = 2.0 ** -8 * (np.abs(ref) + np.abs(y * g)) + 1e-30
+    bound = 2.0 ** -7 * (np.abs(ref) + np.abs(y * g)) + 1e-30
     assert (np.abs(got - ref) <= bound).all()
     assert (got == ref).mean() > 0.98
     assert OO.rel_l2(got - x, ref - x) <= 2e-2
