@@ -421,22 +421,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_fence_after();
       const float scale = qr * ksc_s[j];
       const int valid = p.S - j * 128;   // keys of this tile inside the sequence
-      // pass 1: the row max of the raw scores (keys past S masked in the last tile)
+      // pass 1: the row max of the raw scores (keys past S masked in the last tile).  TMEM loads are software-
+      // pipelined: chunk c + 1 is in flight while chunk c is reduced (tcgen05.wait::ld waits for all of them).
       float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sr[32];
-        tmem_ld32(s_col + c * 32, sr);
+      {
+        uint32_t buf[2][32];
+        tmem_ld32(s_col, buf[0]);
         tmem_ld_wait();
-        if (valid < 128) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (c * 32 + e >= valid) sr[e] = __float_as_uint(-INFINITY);
+        for (int c = 0; c < 4; ++c) {
+          if (c < 3) tmem_ld32(s_col + (c + 1) * 32, buf[(c + 1) & 1]);
+          uint32_t* sr = buf[c & 1];
+          if (valid < 128) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (c * 32 + e >= valid) sr[e] = __float_as_uint(-INFINITY);
+          }
+          float m[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float* f = reinterpret_cast<const float*>(sr) + 8 * k;
+            m[k] = max3(max3(f[0], f[1], f[2]), max3(f[3], f[4], f[5]), fmaxf(f[6], f[7]));
+          }
+          mx = max3(mx, fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+          if (c < 3) tmem_ld_wait();
         }
-        float m = __uint_as_float(sr[0]);
-#pragma unroll
-        for (int e = 1; e < 31; e += 2) m = max3(m, __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]));
-        mx = max3(mx, m, __uint_as_float(sr[31]));
       }
       const float mnew = mx * scale;
       // raise the running max only when a row's max grew by more than tau; the tcgen05 ld/st of O are warp-wide,
@@ -462,30 +471,37 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       const uint64_t scale2 = f32x2_splat(scale), nbias2 = f32x2_splat(kPOffset - m_used);
       float lsum = 0.f;
-      // pass 2: P = exp2(s * scale - m + c) -> e4m3, written over the first 32 columns of S (read chunk c before
-      // writing chunk c's P words, which land in columns the earlier chunks already consumed)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sr[32];
-        tmem_ld32(s_col + c * 32, sr);
+      // pass 2: P = exp2(s * scale - m + c) -> e4m3, written over the first 32 columns of S (chunk c's P words land
+      // in columns 8c..8c+7, which chunk 0 held and which were read before any P was written); loads pipelined as
+      // in pass 1
+      {
+        uint32_t buf[2][32];
+        tmem_ld32(s_col, buf[0]);
         tmem_ld_wait();
-        if (valid < 128) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (c * 32 + e >= valid) sr[e] = __float_as_uint(-INFINITY);
-        }
-        uint32_t pw[8];
-        uint32_t hs = 0;
+        for (int c = 0; c < 4; ++c) {
+          if (c < 3) tmem_ld32(s_col + (c + 1) * 32, buf[(c + 1) & 1]);
+          uint32_t* sr = buf[c & 1];
+          if (valid < 128) {
 #pragma unroll
-        for (int w = 0; w < 8; ++w) {
-          const uint32_t e0 = exp2_pair(__uint_as_float(sr[4 * w]), __uint_as_float(sr[4 * w + 1]), scale2, nbias2);
-          const uint32_t e1 = exp2_pair(__uint_as_float(sr[4 * w + 2]), __uint_as_float(sr[4 * w + 3]), scale2,
-                                        nbias2);
-          hs = hadd2(hs, hadd2(e0, e1));
-          pw[w] = e4m3x4_f16(e0, e1);
+            for (int e = 0; e < 32; ++e)
+              if (c * 32 + e >= valid) sr[e] = __float_as_uint(-INFINITY);
+          }
+          uint32_t pw[8];
+          uint32_t hs0 = 0, hs1 = 0;
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            const uint32_t e0 = exp2_pair(__uint_as_float(sr[4 * w]), __uint_as_float(sr[4 * w + 1]), scale2, nbias2);
+            const uint32_t e1 =
+                exp2_pair(__uint_as_float(sr[4 * w + 2]), __uint_as_float(sr[4 * w + 3]), scale2, nbias2);
+            hs0 = hadd2(hs0, e0);
+            hs1 = hadd2(hs1, e1);
+            pw[w] = e4m3x4_f16(e0, e1);
+          }
+          lsum += hsum2_f32(hadd2(hs0, hs1));
+          tmem_st8(s_col + c * 8, pw);
+          if (c < 3) tmem_ld_wait();
         }
-        lsum += hsum2_f32(hs);
-        tmem_st8(s_col + c * 8, pw);
       }
       l += lsum;
       tmem_st_wait();

@@ -7,7 +7,7 @@
 //
 // CTA tile 128 x BN (BN = 256 or 128), K tile 256 elements (128 bytes, one 128-byte swizzle row), 4-stage smem ring.
 // Warp 0: TMA producer.  Warp 1: TMEM owner and MMA issuer (one thread).  Warps 2-5: epilogue, warp w reading TMEM
-// lanes 32 * (w % 4) .. +31, i.e. one output row per thread.
+// lanes 32 * (w % 4) .. +31, i.e. one output row per thread.  Persistent over output tiles.
 #pragma once
 
 #include "common.cuh"
@@ -62,6 +62,10 @@ __device__ __forceinline__ float act_apply(int kind, float g, float u) {
   return kind ? silu_mul(g, u) : gelu_tanh_f(u);
 }
 
+// Persistent: grid = min(#tiles, #SMs) CTAs walk the tiles round-robin (tile t -> m block t / tiles_n, n block
+// t % tiles_n, so the CTAs in flight share A rows and stream B through L2).  One accumulator in TMEM: the epilogue
+// warps first copy it out as packed bf16 (every epilogue rounds y to bf16 first) and hand TMEM back to the MMA warp,
+// then do the global-memory half of the epilogue while the next tile's MMAs run.
 template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -72,12 +76,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
   uint64_t* empty = full + kGemmStages;
   uint64_t* acc_full = empty + kGemmStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* acc_empty = acc_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m_blk = blockIdx.y, m0 = m_blk * 128;
   const int KT = p.K >> 8;
   const int kblocks64 = p.K >> 6;
+  const int tiles_n = p.N / BN;
+  const int tiles = ((p.M + 127) >> 7) * tiles_n;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kGemmStages; ++s) {
@@ -85,6 +91,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 4);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -97,105 +104,128 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       prefetch_tmap(&tmA);
       prefetch_tmap(&tmB);
-      for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % kGemmStages;
-        const uint32_t ph = (kt / kGemmStages) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, 101)) break;
-        uint8_t* st = smem + s * L::STAGE_BYTES;
-        mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
-        tma_load_2d(st, &tmA, kt * 128, m0, &full[s]);
-        tma_load_2d(st + L::A_BYTES, &tmB, kt * 128, n0, &full[s]);
-        bulk_load(st + L::A_BYTES + L::B_BYTES, p.sfa + ((size_t)m_blk * kblocks64 + kt * 4) * 512, 2048, &full[s]);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+        const int m_blk = t / tiles_n, n0 = (t % tiles_n) * BN;
+        for (int kt = 0; kt < KT; ++kt, ++it) {
+          const int s = it % kGemmStages;
+          const uint32_t ph = (it / kGemmStages) & 1;
+          if (!(ok = mbar_wait(&empty[s], ph ^ 1, 101))) break;
+          uint8_t* st = smem + s * L::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
+          tma_load_2d(st, &tmA, kt * 128, m_blk * 128, &full[s]);
+          tma_load_2d(st + L::A_BYTES, &tmB, kt * 128, n0, &full[s]);
+          bulk_load(st + L::A_BYTES + L::B_BYTES, p.sfa + ((size_t)m_blk * kblocks64 + kt * 4) * 512, 2048,
+                    &full[s]);
 #pragma unroll
-        for (int nb = 0; nb < BN / 128; ++nb)
-          bulk_load(st + L::A_BYTES + L::B_BYTES + L::SFA_BYTES + nb * 2048,
-                    p.sfb + ((size_t)(n0 / 128 + nb) * kblocks64 + kt * 4) * 512, 2048, &full[s]);
+          for (int nb = 0; nb < BN / 128; ++nb)
+            bulk_load(st + L::A_BYTES + L::B_BYTES + L::SFA_BYTES + nb * 2048,
+                      p.sfb + ((size_t)(n0 / 128 + nb) * kblocks64 + kt * 4) * 512, 2048, &full[s]);
+        }
       }
     }
   } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_nvfp4(128, BN);
-      for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % kGemmStages;
-        const uint32_t ph = (kt / kGemmStages) & 1;
-        if (!mbar_wait(&full[s], ph, 102)) break;
+      uint32_t it = 0, ti = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x, ++ti) {
+        if (ti > 0 && !(ok = mbar_wait(acc_empty, (ti - 1) & 1, 104))) break;
         tc_fence_after();
-        uint8_t* st = smem + s * L::STAGE_BYTES;
-        const uint32_t a_s = smem_u32(st), b_s = smem_u32(st + L::A_BYTES);
-        const uint32_t sfa_s = smem_u32(st + L::A_BYTES + L::B_BYTES);
-        const uint32_t sfb_s = sfa_s + L::SFA_BYTES;
-        const uint32_t sf_t = tmem + s * L::SF_COLS;   // this stage's scale-factor buffer
+        for (int kt = 0; kt < KT; ++kt, ++it) {
+          const int s = it % kGemmStages;
+          const uint32_t ph = (it / kGemmStages) & 1;
+          if (!(ok = mbar_wait(&full[s], ph, 102))) break;
+          tc_fence_after();
+          uint8_t* st = smem + s * L::STAGE_BYTES;
+          const uint32_t a_s = smem_u32(st), b_s = smem_u32(st + L::A_BYTES);
+          const uint32_t sfa_s = smem_u32(st + L::A_BYTES + L::B_BYTES);
+          const uint32_t sfb_s = sfa_s + L::SFA_BYTES;
+          const uint32_t sf_t = tmem + s * L::SF_COLS;   // this stage's scale-factor buffer
 #pragma unroll
-        for (int kb = 0; kb < 4; ++kb) {
-          tmem_cp_32x128b_x4(sf_t + L::SFA_COL + 4 * kb, sdesc_sf_atom(sfa_s + kb * 512));
+          for (int kb = 0; kb < 4; ++kb) {
+            tmem_cp_32x128b_x4(sf_t + L::SFA_COL + 4 * kb, sdesc_sf_atom(sfa_s + kb * 512));
 #pragma unroll
-          for (int nb = 0; nb < BN / 128; ++nb)
-            tmem_cp_32x128b_x4(sf_t + L::SFB_COL + (BN / 32) * kb + 4 * nb, sdesc_sf_atom(sfb_s + nb * 2048 + kb * 512));
+            for (int nb = 0; nb < BN / 128; ++nb)
+              tmem_cp_32x128b_x4(sf_t + L::SFB_COL + (BN / 32) * kb + 4 * nb,
+                                 sdesc_sf_atom(sfb_s + nb * 2048 + kb * 512));
+          }
+#pragma unroll
+          for (int kb = 0; kb < 4; ++kb)
+            mma_nvfp4(tmem, sdesc_kmajor_sw128(a_s + kb * 32), sdesc_kmajor_sw128(b_s + kb * 32), idesc,
+                      sf_t + L::SFA_COL + 4 * kb, sf_t + L::SFB_COL + (BN / 32) * kb, (kt | kb) != 0);
+          tc_commit(&empty[s]);
         }
-#pragma unroll
-        for (int kb = 0; kb < 4; ++kb) {
-          mma_nvfp4(tmem, sdesc_kmajor_sw128(a_s + kb * 32), sdesc_kmajor_sw128(b_s + kb * 32), idesc,
-                    sf_t + L::SFA_COL + 4 * kb, sf_t + L::SFB_COL + (BN / 32) * kb, (kt | kb) != 0);
-        }
-        tc_commit(&empty[s]);
+        tc_commit(acc_full);
       }
-      tc_commit(acc_full);
     }
   } else {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;
-    const int row = m0 + q * 32 + lane;
-    const bool live = row < p.M;
-    __nv_bfloat16* __restrict__ xrow = nullptr;
-    const float* __restrict__ gate = nullptr;
-    if (p.epi == H3_EPI_GATE_RESID && live) {
-      // the residual tile is read after the mainloop: pull this row's 2 * BN bytes into L2 while the MMAs run
-      xrow = p.x + (size_t)row * p.ldx + n0;
-      gate = p.mod + ((size_t)p.idx[row] * 6 + 3 * p.gate_part + 2) * p.N + n0;
+    const float alpha = p.a_slot->act * p.g_b;
+    const float inv_q = p.epi == H3_EPI_ACT_Q ? __fdiv_rn(1.0f, p.q_slot->act) : 0.f;
+    const int F = p.act_kind ? (p.N >> 1) : p.N;   // activation width (ACT_*)
+    float amax = 0.f;
+    uint32_t ti = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++ti) {
+      const int m_blk = t / tiles_n, n0 = (t % tiles_n) * BN;
+      const int row = m_blk * 128 + q * 32 + lane;
+      const bool live = row < p.M;
+      __nv_bfloat16* __restrict__ xrow = nullptr;
+      const float* __restrict__ gate = nullptr;
+      if (p.epi == H3_EPI_GATE_RESID && live) {
+        // pull this row's slice of the residual into L2 while the tile's MMAs run
+        xrow = p.x + (size_t)row * p.ldx + n0;
+        gate = p.mod + ((size_t)p.idx[row] * 6 + 3 * p.gate_part + 2) * p.N + n0;
 #pragma unroll
-      for (int b = 0; b < BN * 2; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"((const char*)xrow + b));
-    }
-    const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, 103));   // tcgen05.ld below is warp-wide
-    tc_fence_after();
-    if (ok) {
-      const float alpha = p.a_slot->act * p.g_b;
-      float inv_q = 0.f;
-      if (p.epi == H3_EPI_ACT_Q) inv_q = __fdiv_rn(1.0f, p.q_slot->act);
-      float amax = 0.f;
-      const int F = p.act_kind ? (p.N >> 1) : p.N;   // activation width (ACT_*)
-#pragma unroll 1
+        for (int b = 0; b < BN * 2; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"((const char*)xrow + b));
+      }
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, ti & 1, 103));   // tcgen05.ld is warp-wide
+      if (!ok) break;
+      tc_fence_after();
+      // phase 1: accumulator -> bf16(acc * gA * gB + bias) in registers, then TMEM goes back to the MMA warp
+      uint32_t hold[BN / 2];
+#pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
-        // issue this chunk's global loads (residual, gate) before the TMEM load so their latency overlaps it
-        uint4 xu[4];
-        float4 ga[8];
-        if (xrow) {
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float v0 = __uint_as_float(r[2 * j]) * alpha, v1 = __uint_as_float(r[2 * j + 1]) * alpha;
+          if (p.bias) {
+            v0 += p.bias[n0 + c * 32 + 2 * j];
+            v1 += p.bias[n0 + c * 32 + 2 * j + 1];
+          }
+          hold[c * 16 + j] = pack_bf16(v0, v1);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
+      if (!live) continue;
+      // phase 2: the global-memory half, overlapping the next tile's mainloop
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        const int nc = n0 + c * 32;
+        const uint32_t* y = hold + c * 16;   // 32 bf16 values, columns nc..nc+31
+        if (p.epi == H3_EPI_STORE) {
+          uint4* o = reinterpret_cast<uint4*>(p.out + (size_t)row * p.ldo + nc);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) o[j] = make_uint4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+        } else if (p.epi == H3_EPI_GATE_RESID) {
+          uint4 xu[4];
+          float4 ga[8];
 #pragma unroll
           for (int j = 0; j < 4; ++j) xu[j] = reinterpret_cast<const uint4*>(xrow + c * 32)[j];
 #pragma unroll
           for (int j = 0; j < 8; ++j) ga[j] = reinterpret_cast<const float4*>(gate + c * 32)[j];
-        }
-        __syncwarp();
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, r);
-        tmem_ld_wait();
-        const int nc = n0 + c * 32;
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          v[j] = __uint_as_float(r[j]) * alpha;
-          if (p.bias) v[j] += p.bias[nc + j];
-        }
-        if (!live) continue;
-        if (p.epi == H3_EPI_STORE) {
-          uint4* o = reinterpret_cast<uint4*>(p.out + (size_t)row * p.ldo + nc);
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            o[j] = make_uint4(pack_bf16(v[8 * j], v[8 * j + 1]), pack_bf16(v[8 * j + 2], v[8 * j + 3]),
-                              pack_bf16(v[8 * j + 4], v[8 * j + 5]), pack_bf16(v[8 * j + 6], v[8 * j + 7]));
-        } else if (p.epi == H3_EPI_GATE_RESID) {
           const float* g = reinterpret_cast<const float*>(ga);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -203,54 +233,57 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int k = 8 * j + 2 * e;
-              float lo = __fadd_rn(bf16_lo(xw[e]), __fmul_rn(bf16_round(v[k]), g[k]));
-              float hi = __fadd_rn(bf16_hi(xw[e]), __fmul_rn(bf16_round(v[k + 1]), g[k + 1]));
+              const uint32_t yw = y[k >> 1];
+              float lo = __fadd_rn(bf16_lo(xw[e]), __fmul_rn(bf16_lo(yw), g[k]));
+              float hi = __fadd_rn(bf16_hi(xw[e]), __fmul_rn(bf16_hi(yw), g[k + 1]));
               xw[e] = pack_bf16(lo, hi);
             }
           }
 #pragma unroll
           for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(xrow + c * 32)[j] = xu[j];
         } else {
-          // activation: gelu -> 32 outputs at columns nc.., swiglu -> 16 outputs at columns nc / 2..
-          float a[32];
-          const int na = p.act_kind ? 16 : 32;
-          const int fc = p.act_kind ? (nc >> 1) : nc;
+          // activation, one 16-wide NVFP4 group at a time: gelu -> groups at columns nc, nc + 16;
+          // swiglu (16-column interleaved [gate | up]) -> one group at column nc / 2
+          const int ngroups = p.act_kind ? 1 : 2;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (j < na) {
-              float y = p.act_kind ? act_apply(1, bf16_round(v[j]), bf16_round(v[j + 16]))
-                                   : act_apply(0, 0.f, bf16_round(v[j]));
-              a[j] = bf16_round(y);
-              amax = fmaxf(amax, fabsf(a[j]));
-            } else {
-              a[j] = 0.f;
+          for (int gi = 0; gi < 2; ++gi) {
+            if (gi >= ngroups) break;
+            const int col = (p.act_kind ? (nc >> 1) : nc) + gi * 16;
+            float a16[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int j = gi * 16 + e;
+              const float u = (j & 1) ? bf16_hi(y[j >> 1]) : bf16_lo(y[j >> 1]);
+              float av;
+              if (p.act_kind) {
+                const uint32_t uw = y[(e + 16) >> 1];
+                av = act_apply(1, u, (e & 1) ? bf16_hi(uw) : bf16_lo(uw));
+              } else {
+                av = act_apply(0, 0.f, u);
+              }
+              a16[e] = bf16_round(av);
+              amax = fmaxf(amax, fabsf(a16[e]));
             }
-          }
-          if (p.out) {
-            uint4* o = reinterpret_cast<uint4*>(p.out + (size_t)row * p.ldo + fc);
-            for (int j = 0; j < na / 8; ++j)
-              o[j] = make_uint4(pack_bf16(a[8 * j], a[8 * j + 1]), pack_bf16(a[8 * j + 2], a[8 * j + 3]),
-                                pack_bf16(a[8 * j + 4], a[8 * j + 5]), pack_bf16(a[8 * j + 6], a[8 * j + 7]));
-          }
-          if (p.epi == H3_EPI_ACT_Q) {
-            const int kgroups = F >> 4;
-            for (int gi = 0; gi < na / 16; ++gi) {
-              float g16[16];
-#pragma unroll
-              for (int e = 0; e < 16; ++e) g16[e] = a[gi * 16 + e];
+            if (p.out) {
+              uint4* o = reinterpret_cast<uint4*>(p.out + (size_t)row * p.ldo + col);
+              o[0] = make_uint4(pack_bf16(a16[0], a16[1]), pack_bf16(a16[2], a16[3]), pack_bf16(a16[4], a16[5]),
+                                pack_bf16(a16[6], a16[7]));
+              o[1] = make_uint4(pack_bf16(a16[8], a16[9]), pack_bf16(a16[10], a16[11]), pack_bf16(a16[12], a16[13]),
+                                pack_bf16(a16[14], a16[15]));
+            }
+            if (p.epi == H3_EPI_ACT_Q) {
               uint32_t cw[2];
-              uint32_t sfb = quant_group16(g16, inv_q, cw);
-              const int col = fc + gi * 16;
+              const uint32_t sfb = quant_group16(a16, inv_q, cw);
               *reinterpret_cast<uint2*>(p.qcodes + (size_t)row * (F >> 1) + (col >> 1)) = make_uint2(cw[0], cw[1]);
-              p.qsf[sf_tiled_offset(row, col >> 4, kgroups)] = (uint8_t)sfb;
+              p.qsf[sf_tiled_offset(row, col >> 4, F >> 4)] = (uint8_t)sfb;
             }
           }
         }
       }
-      if (p.q_slot && (p.epi == H3_EPI_ACT_BF16 || p.epi == H3_EPI_ACT_Q)) {
-        amax = warp_max(amax);
-        if (lane == 0) atomic_max_pos(&p.q_slot->amax, amax);
-      }
+    }
+    if (p.q_slot && (p.epi == H3_EPI_ACT_BF16 || p.epi == H3_EPI_ACT_Q)) {
+      amax = warp_max(amax);
+      if (lane == 0) atomic_max_pos(&p.q_slot->amax, amax);
     }
   }
   tc_fence_before();

@@ -87,6 +87,20 @@ int smem_optin(K kernel, int bytes, unsigned* done_mask, const char* what) {
 
 unsigned g_optin_gemm256 = 0, g_optin_gemm128 = 0, g_optin_attn = 0;
 
+// Streaming multiprocessors of the current device (cached per device).
+int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 struct AttnWs {
@@ -295,7 +309,8 @@ int h3_gemm_nvfp4(const uint8_t* a_codes, const uint8_t* a_sf, const H3ScaleSlot
   if (rc) return rc;
   rc = make_map_u8(&tb, b_codes, K / 2, N, K / 2, 128, BN, "h3_gemm_nvfp4(B)");
   if (rc) return rc;
-  dim3 grid(N / BN, (M + 127) / 128);
+  const int tiles = (N / BN) * ((M + 127) / 128);
+  const int grid = tiles < num_sms() ? tiles : num_sms();
   if (BN == 256) {
     rc = smem_optin(gemm_nvfp4_kernel<256>, GemmSmem<256>::TOTAL, &g_optin_gemm256, "h3_gemm_nvfp4");
     if (rc) return rc;
