@@ -226,7 +226,11 @@ struct AttnArgs {
 };
 
 constexpr int kAttnStages = 3;
-constexpr int kAttnThreads = 320;   // warps 0-3: softmax of query tile 0, 4-7: tile 1, 8: TMA, 9: MMA
+// warps 0-15: softmax, warp w on query tile w / 8, keys 64 * (w / 4 % 2) .. +63 of each KV tile, TMEM lane quadrant
+// w % 4; warp 16: TMA; warp 17: MMA.  Two warps share each row (one per half of the keys): an FP8 tile gives the
+// softmax only about half the MMA time a bf16 tile does, so each row's work is split.
+constexpr int kAttnThreads = 576;
+constexpr int kProdWarp = 16, kMmaWarp = 17;
 constexpr float kTau = 2.0f;        // running-max lag allowed before O is rescaled (log2 units)
 constexpr float kPOffset = 8.807354922057604f - kTau;   // log2(448) - tau
 struct AttnSmem {
@@ -235,7 +239,9 @@ struct AttnSmem {
   static constexpr int KV_OFF = 2 * TILE;               // per stage: K, V^T
   static constexpr int KSC_OFF = KV_OFF + kAttnStages * 2 * TILE;   // this head's K-block scales
   static constexpr int MAX_KBLK = 2048;                                // sequences up to 262,144 tokens
-  static constexpr int BAR_OFF = KSC_OFF + MAX_KBLK * 4;
+  static constexpr int XCH_OFF = KSC_OFF + MAX_KBLK * 4;          // row-max exchange [2 parities][2 tiles][2][128]
+  static constexpr int LX_OFF = XCH_OFF + 2 * 2 * 2 * 128 * 4;     // row-sum exchange [2 tiles][2][128]
+  static constexpr int BAR_OFF = LX_OFF + 2 * 2 * 128 * 4;
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;
 };
 
@@ -317,12 +323,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], 256);
     }
     mbar_init(o_done, 1);
     fence_barrier_init();
   }
-  if (warp == 9) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -332,7 +338,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t tmem = *tmem_slot;
   // TMEM columns: S0 [0, 128), S1 [128, 256), O0 [256, 384), O1 [384, 512); P_i overwrites S_i's first 32 columns.
 
-  if (warp == 8) {
+  if (warp == kProdWarp) {
     if (lane == 0) {
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
@@ -351,7 +357,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tma_load_2d(kv + L::TILE, &tmV, j * 128, h * 128, &v_full[st]);
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == kMmaWarp) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_fp8(128, 128);
       const uint32_t qs0 = smem_u32(smem + L::Q_OFF), qs1 = qs0 + L::TILE;
@@ -362,12 +368,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int kb = 0; kb < 4; ++kb)
           mma_fp8_ss(tmem + i * 128, sdesc_kmajor_sw128(qs + kb * 32), sdesc_kmajor_sw128(ks + kb * 32), idesc, kb != 0);
       };
+      // P of keys 32 kb .. 32 kb + 31 sits in TMEM columns 64 (kb / 2) + 8 (kb % 2) of S_i (each half of the
+      // keys writes its P into its own S columns)
       auto issue_pv = [&](int i, int st, int j) {
         const uint32_t vs = smem_u32(smem + L::KV_OFF + st * 2 * L::TILE + L::TILE);
 #pragma unroll
         for (int kb = 0; kb < 4; ++kb)
-          mma_fp8_ts(tmem + 256 + i * 128, tmem + i * 128 + kb * 8, sdesc_kmajor_sw128(vs + kb * 32), idesc,
-                     (j | kb) != 0);
+          mma_fp8_ts(tmem + 256 + i * 128, tmem + i * 128 + (kb >> 1) * 64 + (kb & 1) * 8,
+                     sdesc_kmajor_sw128(vs + kb * 32), idesc, (j | kb) != 0);
       };
       bool ok = mbar_wait(q_full, 0, 202) && mbar_wait(&k_full[0], 0, 203);
       if (ok) {
@@ -403,14 +411,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_commit(o_done);
     }
   } else {
-    // ------------------------------------------------------------------ softmax warpgroups
-    const int i = warp >> 2;          // query tile
+    // ------------------------------------------------------------------ softmax warps
+    const int i = warp >> 3;          // query tile
+    const int hf = (warp >> 2) & 1;   // which 64 keys of each KV tile (and which 64 columns of O)
     const int qd = warp & 3;          // TMEM lane quadrant
     const int r = qd * 32 + lane;
     const int query = q0 + i * 128 + r;
     const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
     const uint32_t s_col = tmem + lane_off + i * 128;
-    const uint32_t o_col = tmem + lane_off + 256 + i * 128;
+    const uint32_t o_col = tmem + lane_off + 256 + i * 128 + hf * 64;
+    const int bar_id = 1 + i * 4 + qd;   // named barrier of the warp pair (w, w ^ 4) sharing these rows
+    float* xch = reinterpret_cast<float*>(smem + L::XCH_OFF);
+    float* lx = reinterpret_cast<float*>(smem + L::LX_OFF);
     const float qr = p.qscale[(size_t)h * p.SP + query];
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
@@ -420,42 +432,42 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const float scale = qr * ksc_s[j];
-      const int valid = p.S - j * 128;   // keys of this tile inside the sequence
-      // pass 1: the row max of the raw scores (keys past S masked in the last tile).  TMEM loads are software-
-      // pipelined: chunk c + 1 is in flight while chunk c is reduced (tcgen05.wait::ld waits for all of them).
-      float mx = -INFINITY;
-      {
-        uint32_t buf[2][32];
-        tmem_ld32(s_col, buf[0]);
+      const int valid = p.S - j * 128 - hf * 64;   // keys of this half inside the sequence
+      // pass 1: this half's row max (keys past S masked in the last tile), then the pair's max through smem
+      float mh = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t sr[32];
+        tmem_ld32(s_col + hf * 64 + c * 32, sr);
         tmem_ld_wait();
+        if (valid < 64) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          if (c < 3) tmem_ld32(s_col + (c + 1) * 32, buf[(c + 1) & 1]);
-          uint32_t* sr = buf[c & 1];
-          if (valid < 128) {
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (c * 32 + e >= valid) sr[e] = __float_as_uint(-INFINITY);
-          }
-          float m[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float* f = reinterpret_cast<const float*>(sr) + 8 * k;
-            m[k] = max3(max3(f[0], f[1], f[2]), max3(f[3], f[4], f[5]), fmaxf(f[6], f[7]));
-          }
-          mx = max3(mx, fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
-          if (c < 3) tmem_ld_wait();
+          for (int e = 0; e < 32; ++e)
+            if (c * 32 + e >= valid) sr[e] = __float_as_uint(-INFINITY);
         }
+        float m[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t* f = sr + 8 * k;
+          m[k] = max3(max3(__uint_as_float(f[0]), __uint_as_float(f[1]), __uint_as_float(f[2])),
+                      max3(__uint_as_float(f[3]), __uint_as_float(f[4]), __uint_as_float(f[5])),
+                      fmaxf(__uint_as_float(f[6]), __uint_as_float(f[7])));
+        }
+        mh = max3(mh, fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
       }
+      float* xs = xch + ((j & 1) * 2 + i) * 256;
+      xs[hf * 128 + r] = mh;
+      asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
+      const float mx = fmaxf(mh, xs[(hf ^ 1) * 128 + r]);
       const float mnew = mx * scale;
       // raise the running max only when a row's max grew by more than tau; the tcgen05 ld/st of O are warp-wide,
-      // so a warp rescales when any of its rows must (the others multiply by 1)
+      // so a warp rescales when any of its rows must (the others multiply by 1); each half rescales its 64 columns
       const bool need = mnew > m_used + kTau;
       float alpha = 1.0f;
       if (need && j > 0) alpha = ex2(m_used - mnew);
       if (j > 0 && __any_sync(0xffffffffu, need)) {
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t o[32];
           tmem_ld32(o_col + c * 32, o);
           tmem_ld_wait();
@@ -470,54 +482,48 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         m_used = mnew;
       }
       const uint64_t scale2 = f32x2_splat(scale), nbias2 = f32x2_splat(kPOffset - m_used);
-      float lsum = 0.f;
-      // pass 2: P = exp2(s * scale - m + c) -> e4m3, written over the first 32 columns of S (chunk c's P words land
-      // in columns 8c..8c+7, which chunk 0 held and which were read before any P was written); loads pipelined as
-      // in pass 1
-      {
-        uint32_t buf[2][32];
-        tmem_ld32(s_col, buf[0]);
+      // pass 2: P = exp2(s * scale - m + c) -> e4m3 into this half's own S columns 64 hf .. 64 hf + 15 (chunk c's P
+      // words overwrite columns of chunk 0, which was read first)
+      uint32_t hs0 = 0, hs1 = 0;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t sr[32];
+        tmem_ld32(s_col + hf * 64 + c * 32, sr);
         tmem_ld_wait();
+        if (valid < 64) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          if (c < 3) tmem_ld32(s_col + (c + 1) * 32, buf[(c + 1) & 1]);
-          uint32_t* sr = buf[c & 1];
-          if (valid < 128) {
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (c * 32 + e >= valid) sr[e] = __float_as_uint(-INFINITY);
-          }
-          uint32_t pw[8];
-          uint32_t hs0 = 0, hs1 = 0;
-#pragma unroll
-          for (int w = 0; w < 8; ++w) {
-            const uint32_t e0 = exp2_pair(__uint_as_float(sr[4 * w]), __uint_as_float(sr[4 * w + 1]), scale2, nbias2);
-            const uint32_t e1 =
-                exp2_pair(__uint_as_float(sr[4 * w + 2]), __uint_as_float(sr[4 * w + 3]), scale2, nbias2);
-            hs0 = hadd2(hs0, e0);
-            hs1 = hadd2(hs1, e1);
-            pw[w] = e4m3x4_f16(e0, e1);
-          }
-          lsum += hsum2_f32(hadd2(hs0, hs1));
-          tmem_st8(s_col + c * 8, pw);
-          if (c < 3) tmem_ld_wait();
+          for (int e = 0; e < 32; ++e)
+            if (c * 32 + e >= valid) sr[e] = __float_as_uint(-INFINITY);
         }
+        uint32_t pw[8];
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          const uint32_t e0 = exp2_pair(__uint_as_float(sr[4 * w]), __uint_as_float(sr[4 * w + 1]), scale2, nbias2);
+          const uint32_t e1 = exp2_pair(__uint_as_float(sr[4 * w + 2]), __uint_as_float(sr[4 * w + 3]), scale2, nbias2);
+          hs0 = hadd2(hs0, e0);
+          hs1 = hadd2(hs1, e1);
+          pw[w] = e4m3x4_f16(e0, e1);
+        }
+        tmem_st8(s_col + hf * 64 + c * 8, pw);
       }
-      l += lsum;
+      l += hsum2_f32(hadd2(hs0, hs1));
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[i]);
     }
-    // ---- epilogue: O / l * vscale -> bf16
+    // ---- epilogue: row sum of both halves, then this half's 64 columns of O / l * vscale -> bf16
+    lx[(i * 2 + hf) * 128 + r] = l;
+    asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
+    const float lt = l + lx[(i * 2 + (hf ^ 1)) * 128 + r];
     ok = ok && mbar_wait(o_done, 0, 212);
     ok = __all_sync(0xffffffffu, ok);
     if (ok) {
       tc_fence_after();
-      const float inv_l = 1.0f / l;
-      const float* vs = p.vscale + h * 128;
-      __nv_bfloat16* dst = p.out + (long long)query * p.ldo + h * 128;
+      const float inv_l = 1.0f / lt;
+      const float* vs = p.vscale + h * 128 + hf * 64;
+      __nv_bfloat16* dst = p.out + (long long)query * p.ldo + h * 128 + hf * 64;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t o[32];
         __syncwarp();
         tmem_ld32(o_col + c * 32, o);
@@ -539,7 +545,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 9) tmem_dealloc(tmem, 512);
+  if (warp == kMmaWarp) tmem_dealloc(tmem, 512);
 }
 
 }  // namespace h3

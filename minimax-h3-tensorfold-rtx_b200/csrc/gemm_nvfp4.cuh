@@ -66,7 +66,30 @@ __device__ __forceinline__ float act_apply(int kind, float g, float u) {
 // t % tiles_n, so the CTAs in flight share A rows and stream B through L2).  One accumulator in TMEM: the epilogue
 // warps first copy it out as packed bf16 (every epilogue rounds y to bf16 first) and hand TMEM back to the MMA warp,
 // then do the global-memory half of the epilogue while the next tile's MMAs run.
-template <int BN>
+// The 16 packed words (32 bf16 values) of chunk c of the staged accumulator row; a switch keeps `hold` in registers
+// while the chunk loop itself stays rolled (small code for the heavy epilogues).
+template <int K, int N>
+__device__ __forceinline__ void copy_chunk(const uint32_t (&hold)[N], uint32_t (&y)[16]) {
+  if constexpr (K < N / 16) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) y[j] = hold[K * 16 + j];
+  }
+}
+template <int N>
+__device__ __forceinline__ void chunk_words(const uint32_t (&hold)[N], int c, uint32_t (&y)[16]) {
+  switch (c) {
+    case 0: copy_chunk<0>(hold, y); break;
+    case 1: copy_chunk<1>(hold, y); break;
+    case 2: copy_chunk<2>(hold, y); break;
+    case 3: copy_chunk<3>(hold, y); break;
+    case 4: copy_chunk<4>(hold, y); break;
+    case 5: copy_chunk<5>(hold, y); break;
+    case 6: copy_chunk<6>(hold, y); break;
+    default: copy_chunk<7>(hold, y); break;
+  }
+}
+
+template <int BN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const GemmArgs p) {
@@ -169,7 +192,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;
     const float alpha = p.a_slot->act * p.g_b;
-    const float inv_q = p.epi == H3_EPI_ACT_Q ? __fdiv_rn(1.0f, p.q_slot->act) : 0.f;
+    const float inv_q = EPI == H3_EPI_ACT_Q ? __fdiv_rn(1.0f, p.q_slot->act) : 0.f;
     const int F = p.act_kind ? (p.N >> 1) : p.N;   // activation width (ACT_*)
     float amax = 0.f;
     uint32_t ti = 0;
@@ -179,7 +202,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const bool live = row < p.M;
       __nv_bfloat16* __restrict__ xrow = nullptr;
       const float* __restrict__ gate = nullptr;
-      if (p.epi == H3_EPI_GATE_RESID && live) {
+      if (EPI == H3_EPI_GATE_RESID && live) {
         // pull this row's slice of the residual into L2 while the tile's MMAs run
         xrow = p.x + (size_t)row * p.ldx + n0;
         gate = p.mod + ((size_t)p.idx[row] * 6 + 3 * p.gate_part + 2) * p.N + n0;
@@ -211,15 +234,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (lane == 0) mbar_arrive(acc_empty);
       if (!live) continue;
       // phase 2: the global-memory half, overlapping the next tile's mainloop
-#pragma unroll
+#pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         const int nc = n0 + c * 32;
-        const uint32_t* y = hold + c * 16;   // 32 bf16 values, columns nc..nc+31
-        if (p.epi == H3_EPI_STORE) {
+        uint32_t y[16];   // 32 bf16 values, columns nc..nc+31
+        chunk_words(hold, c, y);
+        if (EPI == H3_EPI_STORE) {
           uint4* o = reinterpret_cast<uint4*>(p.out + (size_t)row * p.ldo + nc);
 #pragma unroll
           for (int j = 0; j < 4; ++j) o[j] = make_uint4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
-        } else if (p.epi == H3_EPI_GATE_RESID) {
+        } else if (EPI == H3_EPI_GATE_RESID) {
           uint4 xu[4];
           float4 ga[8];
 #pragma unroll
@@ -271,7 +295,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               o[1] = make_uint4(pack_bf16(a16[8], a16[9]), pack_bf16(a16[10], a16[11]), pack_bf16(a16[12], a16[13]),
                                 pack_bf16(a16[14], a16[15]));
             }
-            if (p.epi == H3_EPI_ACT_Q) {
+            if (EPI == H3_EPI_ACT_Q) {
               uint32_t cw[2];
               const uint32_t sfb = quant_group16(a16, inv_q, cw);
               *reinterpret_cast<uint2*>(p.qcodes + (size_t)row * (F >> 1) + (col >> 1)) = make_uint2(cw[0], cw[1]);
@@ -281,7 +305,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
     }
-    if (p.q_slot && (p.epi == H3_EPI_ACT_BF16 || p.epi == H3_EPI_ACT_Q)) {
+    if (p.q_slot && (EPI == H3_EPI_ACT_BF16 || EPI == H3_EPI_ACT_Q)) {
       amax = warp_max(amax);
       if (lane == 0) atomic_max_pos(&p.q_slot->amax, amax);
     }

@@ -85,7 +85,7 @@ int smem_optin(K kernel, int bytes, unsigned* done_mask, const char* what) {
   return H3_OK;
 }
 
-unsigned g_optin_gemm256 = 0, g_optin_gemm128 = 0, g_optin_attn = 0;
+unsigned g_optin_attn = 0;
 
 // Streaming multiprocessors of the current device (cached per device).
 int num_sms() {
@@ -102,6 +102,30 @@ int num_sms() {
 }
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+unsigned g_optin_gemm[2][4] = {};
+
+template <int BN, int EPI>
+int launch_gemm_t(int grid, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& p, cudaStream_t st) {
+  int rc = smem_optin(gemm_nvfp4_kernel<BN, EPI>, GemmSmem<BN>::TOTAL, &g_optin_gemm[BN == 256][EPI], "h3_gemm_nvfp4");
+  if (rc) return rc;
+  gemm_nvfp4_kernel<BN, EPI><<<grid, kGemmThreads, GemmSmem<BN>::TOTAL, st>>>(ta, tb, p);
+  return H3_OK;
+}
+
+int launch_gemm(int BN, int epi, int grid, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& p,
+                cudaStream_t st) {
+  switch (epi + 4 * (BN == 256)) {
+    case 0: return launch_gemm_t<128, H3_EPI_STORE>(grid, ta, tb, p, st);
+    case 1: return launch_gemm_t<128, H3_EPI_GATE_RESID>(grid, ta, tb, p, st);
+    case 2: return launch_gemm_t<128, H3_EPI_ACT_BF16>(grid, ta, tb, p, st);
+    case 3: return launch_gemm_t<128, H3_EPI_ACT_Q>(grid, ta, tb, p, st);
+    case 4: return launch_gemm_t<256, H3_EPI_STORE>(grid, ta, tb, p, st);
+    case 5: return launch_gemm_t<256, H3_EPI_GATE_RESID>(grid, ta, tb, p, st);
+    case 6: return launch_gemm_t<256, H3_EPI_ACT_BF16>(grid, ta, tb, p, st);
+    default: return launch_gemm_t<256, H3_EPI_ACT_Q>(grid, ta, tb, p, st);
+  }
+}
 
 struct AttnWs {
   size_t q8, k8, vt8, qscale, kscale, kmean, vscale, vinv, ksum, vmax, total;
@@ -311,15 +335,8 @@ int h3_gemm_nvfp4(const uint8_t* a_codes, const uint8_t* a_sf, const H3ScaleSlot
   if (rc) return rc;
   const int tiles = (N / BN) * ((M + 127) / 128);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  if (BN == 256) {
-    rc = smem_optin(gemm_nvfp4_kernel<256>, GemmSmem<256>::TOTAL, &g_optin_gemm256, "h3_gemm_nvfp4");
-    if (rc) return rc;
-    gemm_nvfp4_kernel<256><<<grid, kGemmThreads, GemmSmem<256>::TOTAL, S_(stream)>>>(ta, tb, p);
-  } else {
-    rc = smem_optin(gemm_nvfp4_kernel<128>, GemmSmem<128>::TOTAL, &g_optin_gemm128, "h3_gemm_nvfp4");
-    if (rc) return rc;
-    gemm_nvfp4_kernel<128><<<grid, kGemmThreads, GemmSmem<128>::TOTAL, S_(stream)>>>(ta, tb, p);
-  }
+  rc = launch_gemm(BN, epi->kind, grid, ta, tb, p, S_(stream));
+  if (rc) return rc;
   return check_launch("h3_gemm_nvfp4");
 }
 
