@@ -35,16 +35,11 @@ struct QkNormArgs {
   float eps;
 };
 
-__global__ void __launch_bounds__(256) qknorm_rope_kernel(QkNormArgs a) {
-  const int lane = threadIdx.x & 31;
-  const long long wid = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const long long nrows = (long long)a.S * 2 * a.H;
-  if (wid >= nrows) return;
-  const int s = (int)(wid / (2 * a.H));
-  const int rem = (int)(wid % (2 * a.H));
-  const int which = rem / a.H, h = rem % a.H;
-  __nv_bfloat16* row = (which ? a.k : a.q) + (long long)s * a.ld + h * 128;
-  const float* w = which ? a.kw : a.qw;
+// One warp per token: its RoPE matrices are loaded once into registers (lane l's dims 4l..4l+3 need pairs 4l..4l+3
+// when they lie in the first half of the rotated span, 4l - rot/2.. in the second) and applied to the token's 2H head
+// rows, two rows in flight at a time.
+__device__ __forceinline__ void qk_row(__nv_bfloat16* row, const float* w, const float (&f)[4][4], int lane, int half,
+                                       int rot, int src, float eps) {
   uint2 u = *reinterpret_cast<const uint2*>(row + lane * 4);
   float x[4] = {bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y)};
   float ss = 0.f;
@@ -52,33 +47,61 @@ __global__ void __launch_bounds__(256) qknorm_rope_kernel(QkNormArgs a) {
   for (int e = 0; e < 4; ++e) ss = __fadd_rn(ss, __fmul_rn(x[e], x[e]));
 #pragma unroll
   for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), a.eps)));
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), eps)));
   float y[4];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) y[e] = __fmul_rn(__fmul_rn(x[e], r), w[lane * 4 + e]);
+  for (int e = 0; e < 4; ++e) y[e] = __fmul_rn(__fmul_rn(x[e], r), w[e]);
+  float pv[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) pv[e] = __shfl_sync(0xffffffffu, y[e], src);
+  float o[4];
+  const int d0 = lane * 4;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    if (d0 < half)
+      o[e] = __fadd_rn(__fmul_rn(f[e][0], y[e]), __fmul_rn(f[e][1], pv[e]));
+    else if (d0 < rot)
+      o[e] = __fadd_rn(__fmul_rn(f[e][2], pv[e]), __fmul_rn(f[e][3], y[e]));
+    else
+      o[e] = y[e];
+  }
+  *reinterpret_cast<uint2*>(row + lane * 4) = make_uint2(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]));
+}
+
+__global__ void __launch_bounds__(256) qknorm_rope_kernel(QkNormArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int s = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (s >= a.S) return;
   const int half = a.rot >> 1, hq = half >> 2;
   const int d0 = lane * 4;
   int src = lane;
   if (d0 < half) src = lane + hq;
   else if (d0 < a.rot) src = lane - hq;
-  float pv[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) pv[e] = __shfl_sync(0xffffffffu, y[e], src);
-  float o[4];
+  float f[4][4];
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
     const int d = d0 + e;
-    if (d < half) {
-      float4 f = *reinterpret_cast<const float4*>(a.rope + ((size_t)s * half + d) * 4);
-      o[e] = __fadd_rn(__fmul_rn(f.x, y[e]), __fmul_rn(f.y, pv[e]));
-    } else if (d < a.rot) {
-      float4 f = *reinterpret_cast<const float4*>(a.rope + ((size_t)s * half + (d - half)) * 4);
-      o[e] = __fadd_rn(__fmul_rn(f.z, pv[e]), __fmul_rn(f.w, y[e]));
-    } else {
-      o[e] = y[e];
-    }
+    const int pair = d < half ? d : d - half;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (d < a.rot) v = *reinterpret_cast<const float4*>(a.rope + ((size_t)s * half + pair) * 4);
+    f[e][0] = v.x;
+    f[e][1] = v.y;
+    f[e][2] = v.z;
+    f[e][3] = v.w;
   }
-  *reinterpret_cast<uint2*>(row + lane * 4) = make_uint2(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]));
+  float qw[4], kw[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    qw[e] = a.qw[d0 + e];
+    kw[e] = a.kw[d0 + e];
+  }
+  __nv_bfloat16* qrow = a.q + (long long)s * a.ld;
+  __nv_bfloat16* krow = a.k + (long long)s * a.ld;
+#pragma unroll 2
+  for (int h = 0; h < a.H; ++h) {
+    qk_row(qrow + h * 128, qw, f, lane, half, a.rot, src, a.eps);
+    qk_row(krow + h * 128, kw, f, lane, half, a.rot, src, a.eps);
+  }
 }
 
 // ------------------------------------------------------------------------------------------------ prepare
@@ -95,16 +118,41 @@ struct AttnView {
 // Per (128-token block, head): partial channel sums of k and channel maxima of |v| -> part[blk][h][d] (sum) and
 // part[nblk][H][128] + ... (max) in the workspace; fixed order, so the statistics are deterministic.
 __global__ void __launch_bounds__(128) attn_stats_kernel(AttnView a, int S, int H, float* ksum_part, float* vmax_part) {
-  const int blk = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  // thread (g, c8): channels 8 c8 .. 8 c8 + 7 over tokens t0 + g, t0 + g + 8, ... (16-byte loads); the 8 token groups
+  // are combined in a fixed order through shared memory
+  __shared__ float red_s[8][128], red_m[8][128];
+  const int blk = blockIdx.x, h = blockIdx.y;
+  const int c8 = threadIdx.x & 15, g = threadIdx.x >> 4;
   const int t0 = blk * 128, t1 = min(S, t0 + 128);
-  float ks = 0.f, vm = 0.f;
-  for (int t = t0; t < t1; ++t) {
-    const long long off = (long long)t * a.ld + (long long)h * a.hstride + d;
-    ks = __fadd_rn(ks, __bfloat162float(a.k[off]));
-    vm = fmaxf(vm, fabsf(__bfloat162float(a.v[off])));
+  float ks[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, vm[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int t = t0 + g; t < t1; t += 8) {
+    const long long off = (long long)t * a.ld + (long long)h * a.hstride + c8 * 8;
+    const uint4 ku = *reinterpret_cast<const uint4*>(a.k + off);
+    const uint4 vu = *reinterpret_cast<const uint4*>(a.v + off);
+    const uint32_t kw[4] = {ku.x, ku.y, ku.z, ku.w}, vw[4] = {vu.x, vu.y, vu.z, vu.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      ks[2 * j] = __fadd_rn(ks[2 * j], bf16_lo(kw[j]));
+      ks[2 * j + 1] = __fadd_rn(ks[2 * j + 1], bf16_hi(kw[j]));
+      vm[2 * j] = fmaxf(vm[2 * j], fabsf(bf16_lo(vw[j])));
+      vm[2 * j + 1] = fmaxf(vm[2 * j + 1], fabsf(bf16_hi(vw[j])));
+    }
   }
-  ksum_part[((size_t)blk * H + h) * 128 + d] = ks;
-  vmax_part[((size_t)blk * H + h) * 128 + d] = vm;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    red_s[g][c8 * 8 + e] = ks[e];
+    red_m[g][c8 * 8 + e] = vm[e];
+  }
+  __syncthreads();
+  const int d = threadIdx.x;
+  float sum = 0.f, mx = 0.f;
+#pragma unroll
+  for (int gg = 0; gg < 8; ++gg) {
+    sum = __fadd_rn(sum, red_s[gg][d]);
+    mx = fmaxf(mx, red_m[gg][d]);
+  }
+  ksum_part[((size_t)blk * H + h) * 128 + d] = sum;
+  vmax_part[((size_t)blk * H + h) * 128 + d] = mx;
 }
 
 // kmean[h][d] = sum over blocks / S; vscale[h][d] = vmax / 448 (the epilogue's per-channel factor), vinv = 448 / vmax.
@@ -196,10 +244,11 @@ __global__ void __launch_bounds__(128) attn_quant_kernel(AttnView a, int S, int 
     for (int c = 0; c < 8; ++c) dst[c] = make_uint4(outw[4 * c], outw[4 * c + 1], outw[4 * c + 2], outw[4 * c + 3]);
     if (tid == 0) kscale[(size_t)h * (SP / 128) + blk] = kr;
   }
-  // ---- V (per channel), transposed
+  // ---- V (per channel), transposed through shared memory: thread t writes column t of the [128 d][128 t] tile,
+  // then each thread stores one row d with 16-byte writes
   {
+    __shared__ uint32_t vt[128][33];   // [d][t / 4] words, padded
     const float* vi = vinv + h * 128;
-    uint8_t* dst = vt8 + (size_t)h * 128 * SP + t;
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
       uint4 u = live ? *reinterpret_cast<const uint4*>(a.v + base + c * 8) : make_uint4(0, 0, 0, 0);
@@ -207,11 +256,15 @@ __global__ void __launch_bounds__(128) attn_quant_kernel(AttnView a, int S, int 
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int d = c * 8 + 2 * j;
-        uint32_t b = e4m3x2(__fmul_rn(bf16_lo(w[j]), vi[d]), __fmul_rn(bf16_hi(w[j]), vi[d + 1]));
-        dst[(size_t)d * SP] = (uint8_t)(b & 0xFF);
-        dst[(size_t)(d + 1) * SP] = (uint8_t)(b >> 8);
+        const uint32_t b = e4m3x2(__fmul_rn(bf16_lo(w[j]), vi[d]), __fmul_rn(bf16_hi(w[j]), vi[d + 1]));
+        reinterpret_cast<uint8_t*>(&vt[d][0])[tid] = (uint8_t)(b & 0xFF);
+        reinterpret_cast<uint8_t*>(&vt[d + 1][0])[tid] = (uint8_t)(b >> 8);
       }
     }
+    __syncthreads();
+    uint4* dst = reinterpret_cast<uint4*>(vt8 + ((size_t)h * 128 + tid) * SP + (size_t)blk * 128);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) dst[k] = make_uint4(vt[tid][4 * k], vt[tid][4 * k + 1], vt[tid][4 * k + 2], vt[tid][4 * k + 3]);
   }
 }
 
@@ -225,23 +278,25 @@ struct AttnArgs {
   int S, SP, H;
 };
 
-constexpr int kAttnStages = 3;
-// warps 0-15: softmax, warp w on query tile w / 8, keys 64 * (w / 4 % 2) .. +63 of each KV tile, TMEM lane quadrant
-// w % 4; warp 16: TMA; warp 17: MMA.  Two warps share each row (one per half of the keys): an FP8 tile gives the
-// softmax only about half the MMA time a bf16 tile does, so each row's work is split.
+constexpr int kAttnStages = 4;
+// One 128-row query tile per CTA with two S buffers in TMEM, so QK^T of KV tile j + 1 runs on the tensor cores while
+// the softmax of tile j does.  Warps 0-15: softmax, warp w on TMEM lane quadrant w % 4 and keys 32 (w / 4) .. +31 of
+// each KV tile (four warps share each row: an FP8 tile leaves the softmax about half the MMA time a bf16 tile does);
+// warp 16: TMA; warp 17: MMA.
 constexpr int kAttnThreads = 576;
 constexpr int kProdWarp = 16, kMmaWarp = 17;
+constexpr int kQTile = 128;
 constexpr float kTau = 2.0f;        // running-max lag allowed before O is rescaled (log2 units)
 constexpr float kPOffset = 8.807354922057604f - kTau;   // log2(448) - tau
 struct AttnSmem {
   static constexpr int TILE = 128 * 128;
-  static constexpr int Q_OFF = 0;                       // Q0, Q1
-  static constexpr int KV_OFF = 2 * TILE;               // per stage: K, V^T
+  static constexpr int Q_OFF = 0;
+  static constexpr int KV_OFF = TILE;                   // per stage: K, V^T
   static constexpr int KSC_OFF = KV_OFF + kAttnStages * 2 * TILE;   // this head's K-block scales
   static constexpr int MAX_KBLK = 2048;                                // sequences up to 262,144 tokens
-  static constexpr int XCH_OFF = KSC_OFF + MAX_KBLK * 4;          // row-max exchange [2 parities][2 tiles][2][128]
-  static constexpr int LX_OFF = XCH_OFF + 2 * 2 * 2 * 128 * 4;     // row-sum exchange [2 tiles][2][128]
-  static constexpr int BAR_OFF = LX_OFF + 2 * 2 * 128 * 4;
+  static constexpr int XCH_OFF = KSC_OFF + MAX_KBLK * 4;          // row-max exchange [2 parities][4 warps][128]
+  static constexpr int LX_OFF = XCH_OFF + 2 * 4 * 128 * 4;         // row-sum exchange [4 warps][128]
+  static constexpr int BAR_OFF = LX_OFF + 4 * 128 * 4;
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;
 };
 
@@ -302,14 +357,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = k_full + kAttnStages;
   uint64_t* kv_empty = v_full + kAttnStages;
-  uint64_t* s_full = kv_empty + kAttnStages;   // [2]
-  uint64_t* p_full = s_full + 2;               // [2]
-  uint64_t* o_done = p_full + 2;
+  uint64_t* s_full = kv_empty + kAttnStages;   // [2]: QK^T of tile j in S buffer j % 2
+  uint64_t* p_full = s_full + 2;               // [2]: P of tile j written over S buffer j % 2
+  uint64_t* pv_done = p_full + 2;              // one phase per PV of a tile
+  uint64_t* o_done = pv_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y;
-  const int q0 = blockIdx.x * 256;
+  const int q0 = blockIdx.x * kQTile;
   const int nkv = (p.S + 127) / 128;
   float* ksc_s = reinterpret_cast<float*>(smem + L::KSC_OFF);
   for (int i = threadIdx.x; i < nkv; i += blockDim.x) ksc_s[i] = p.kscale[(size_t)h * (p.SP / 128) + i];
@@ -321,10 +377,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 256);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 512);
     }
+    mbar_init(pv_done, 1);
     mbar_init(o_done, 1);
     fence_barrier_init();
   }
@@ -336,16 +393,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: S0 [0, 128), S1 [128, 256), O0 [256, 384), O1 [384, 512); P_i overwrites S_i's first 32 columns.
+  // TMEM columns: S buffer 0 [0, 128), S buffer 1 [128, 256), O [256, 384).  P of keys 32k..32k+31 goes to columns
+  // 32k..32k+7 of its S buffer (the columns the warp owning those keys read).
 
   if (warp == kProdWarp) {
     if (lane == 0) {
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
-      mbar_arrive_expect_tx(q_full, 2 * L::TILE);
+      mbar_arrive_expect_tx(q_full, L::TILE);
       tma_load_2d(smem + L::Q_OFF, &tmQ, 0, h * p.SP + q0, q_full);
-      tma_load_2d(smem + L::Q_OFF + L::TILE, &tmQ, 0, h * p.SP + q0 + 128, q_full);
       for (int j = 0; j < nkv; ++j) {
         const int st = j % kAttnStages;
         const uint32_t ph = (j / kAttnStages) & 1;
@@ -360,90 +417,74 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_fp8(128, 128);
-      const uint32_t qs0 = smem_u32(smem + L::Q_OFF), qs1 = qs0 + L::TILE;
-      auto issue_s = [&](int i, int st) {
+      const uint32_t qs = smem_u32(smem + L::Q_OFF);
+      auto issue_s = [&](int b, int st) {
         const uint32_t ks = smem_u32(smem + L::KV_OFF + st * 2 * L::TILE);
-        const uint32_t qs = i ? qs1 : qs0;
 #pragma unroll
         for (int kb = 0; kb < 4; ++kb)
-          mma_fp8_ss(tmem + i * 128, sdesc_kmajor_sw128(qs + kb * 32), sdesc_kmajor_sw128(ks + kb * 32), idesc, kb != 0);
+          mma_fp8_ss(tmem + b * 128, sdesc_kmajor_sw128(qs + kb * 32), sdesc_kmajor_sw128(ks + kb * 32), idesc, kb != 0);
       };
-      // P of keys 32 kb .. 32 kb + 31 sits in TMEM columns 64 (kb / 2) + 8 (kb % 2) of S_i (each half of the
-      // keys writes its P into its own S columns)
-      auto issue_pv = [&](int i, int st, int j) {
+      auto issue_pv = [&](int b, int st, int j) {
         const uint32_t vs = smem_u32(smem + L::KV_OFF + st * 2 * L::TILE + L::TILE);
 #pragma unroll
         for (int kb = 0; kb < 4; ++kb)
-          mma_fp8_ts(tmem + 256 + i * 128, tmem + i * 128 + (kb >> 1) * 64 + (kb & 1) * 8,
-                     sdesc_kmajor_sw128(vs + kb * 32), idesc, (j | kb) != 0);
+          mma_fp8_ts(tmem + 256, tmem + b * 128 + kb * 32, sdesc_kmajor_sw128(vs + kb * 32), idesc, (j | kb) != 0);
       };
-      bool ok = mbar_wait(q_full, 0, 202) && mbar_wait(&k_full[0], 0, 203);
-      if (ok) {
+      bool ok = mbar_wait(q_full, 0, 202);
+      for (int j = 0; ok && j < 2 && j < nkv; ++j) {   // prologue: S of tiles 0 and 1
+        if (!(ok = mbar_wait(&k_full[j], 0, 203))) break;
         tc_fence_after();
-        issue_s(0, 0);
-        tc_commit(&s_full[0]);
-        issue_s(1, 0);
-        tc_commit(&s_full[1]);
+        issue_s(j, j);
+        tc_commit(&s_full[j]);
       }
       for (int j = 0; ok && j < nkv; ++j) {
-        const int st = j % kAttnStages;
-        const uint32_t ph = (j / kAttnStages) & 1;
-        if (!(ok = mbar_wait(&p_full[0], j & 1, 204) && mbar_wait(&v_full[st], ph, 205))) break;
+        const int b = j & 1, st = j % kAttnStages;
+        if (!(ok = mbar_wait(&p_full[b], (j >> 1) & 1, 204) && mbar_wait(&v_full[st], (j / kAttnStages) & 1, 205)))
+          break;
         tc_fence_after();
-        issue_pv(0, st, j);
-        const bool more = j + 1 < nkv;
-        const int st1 = (j + 1) % kAttnStages;
-        if (more) {
-          if (!(ok = mbar_wait(&k_full[st1], ((j + 1) / kAttnStages) & 1, 206))) break;
-          tc_fence_after();
-          issue_s(0, st1);
-          tc_commit(&s_full[0]);
-        }
-        if (!(ok = mbar_wait(&p_full[1], j & 1, 207))) break;
-        tc_fence_after();
-        issue_pv(1, st, j);
+        issue_pv(b, st, j);
+        tc_commit(pv_done);
         tc_commit(&kv_empty[st]);
-        if (more) {
-          issue_s(1, st1);
-          tc_commit(&s_full[1]);
+        if (j + 2 < nkv) {
+          const int st2 = (j + 2) % kAttnStages;
+          if (!(ok = mbar_wait(&k_full[st2], ((j + 2) / kAttnStages) & 1, 206))) break;
+          tc_fence_after();
+          issue_s(b, st2);   // after PV(j) in issue order, so P(j) is consumed before S(j + 2) overwrites it
+          tc_commit(&s_full[b]);
         }
       }
       tc_commit(o_done);
     }
   } else {
     // ------------------------------------------------------------------ softmax warps
-    const int i = warp >> 3;          // query tile
-    const int hf = (warp >> 2) & 1;   // which 64 keys of each KV tile (and which 64 columns of O)
-    const int qd = warp & 3;          // TMEM lane quadrant
+    const int kq = warp >> 2;        // keys 32 kq .. 32 kq + 31 of each tile, O columns 32 kq .. 32 kq + 31
+    const int qd = warp & 3;         // TMEM lane quadrant
     const int r = qd * 32 + lane;
-    const int query = q0 + i * 128 + r;
+    const int query = q0 + r;
     const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
-    const uint32_t s_col = tmem + lane_off + i * 128;
-    const uint32_t o_col = tmem + lane_off + 256 + i * 128 + hf * 64;
-    const int bar_id = 1 + i * 4 + qd;   // named barrier of the warp pair (w, w ^ 4) sharing these rows
+    const uint32_t o_col = tmem + lane_off + 256 + kq * 32;
+    const int bar_id = 1 + qd;       // named barrier of the four warps sharing these rows
     float* xch = reinterpret_cast<float*>(smem + L::XCH_OFF);
     float* lx = reinterpret_cast<float*>(smem + L::LX_OFF);
     const float qr = p.qscale[(size_t)h * p.SP + query];
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      ok = mbar_wait(&s_full[i], j & 1, 210 + i);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      tc_fence_after();
+      const int b = j & 1;
+      const uint32_t s_col = tmem + lane_off + b * 128 + kq * 32;
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[b], (j >> 1) & 1, 210));
       const float scale = qr * ksc_s[j];
-      const int valid = p.S - j * 128 - hf * 64;   // keys of this half inside the sequence
-      // pass 1: this half's row max (keys past S masked in the last tile), then the pair's max through smem
-      float mh = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t sr[32];
-        tmem_ld32(s_col + hf * 64 + c * 32, sr);
+      const int valid = p.S - j * 128 - kq * 32;   // keys of this warp's slice inside the sequence
+      uint32_t sr[32];
+      float mloc = -INFINITY;
+      if (ok) {
+        tc_fence_after();
+        tmem_ld32(s_col, sr);
         tmem_ld_wait();
-        if (valid < 64) {
+        if (valid < 32) {
 #pragma unroll
           for (int e = 0; e < 32; ++e)
-            if (c * 32 + e >= valid) sr[e] = __float_as_uint(-INFINITY);
+            if (e >= valid) sr[e] = __float_as_uint(-INFINITY);
         }
         float m[4];
 #pragma unroll
@@ -453,91 +494,85 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                       max3(__uint_as_float(f[3]), __uint_as_float(f[4]), __uint_as_float(f[5])),
                       fmaxf(__uint_as_float(f[6]), __uint_as_float(f[7])));
         }
-        mh = max3(mh, fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+        mloc = fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
       }
-      float* xs = xch + ((j & 1) * 2 + i) * 256;
-      xs[hf * 128 + r] = mh;
-      asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
-      const float mx = fmaxf(mh, xs[(hf ^ 1) * 128 + r]);
+      float* xs = xch + (j & 1) * 512;
+      xs[kq * 128 + r] = mloc;
+      // exchange the four partial maxima; the barrier also ANDs the warps' wait results, so the four warps sharing
+      // these rows leave the loop together (a named barrier has no timeout)
+      {
+        uint32_t all;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred p, %2, 128, p;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(all)
+            : "r"((uint32_t)ok), "r"(bar_id)
+            : "memory");
+        ok = all != 0;
+      }
+      if (!ok) break;
+      const float mx = fmaxf(fmaxf(xs[r], xs[128 + r]), fmaxf(xs[256 + r], xs[384 + r]));
       const float mnew = mx * scale;
       // raise the running max only when a row's max grew by more than tau; the tcgen05 ld/st of O are warp-wide,
-      // so a warp rescales when any of its rows must (the others multiply by 1); each half rescales its 64 columns
+      // so a warp rescales when any of its rows must (the others multiply by 1); each warp rescales its 32 columns
+      // once the previous tile's PV has landed
       const bool need = mnew > m_used + kTau;
       float alpha = 1.0f;
       if (need && j > 0) alpha = ex2(m_used - mnew);
       if (j > 0 && __any_sync(0xffffffffu, need)) {
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          uint32_t o[32];
-          tmem_ld32(o_col + c * 32, o);
-          tmem_ld_wait();
+        // a wait that gives up has recorded the error; the warp stays in step with its partners
+        __all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, 213));
+        tc_fence_after();
+        uint32_t o[32];
+        tmem_ld32(o_col, o);
+        tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st32(o_col + c * 32, o);
-        }
-        tmem_st_wait();
+        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+        tmem_st32(o_col, o);
       }
       if (need) {
         l *= alpha;
         m_used = mnew;
       }
       const uint64_t scale2 = f32x2_splat(scale), nbias2 = f32x2_splat(kPOffset - m_used);
-      // pass 2: P = exp2(s * scale - m + c) -> e4m3 into this half's own S columns 64 hf .. 64 hf + 15 (chunk c's P
-      // words overwrite columns of chunk 0, which was read first)
+      uint32_t pw[8];
       uint32_t hs0 = 0, hs1 = 0;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t sr[32];
-        tmem_ld32(s_col + hf * 64 + c * 32, sr);
-        tmem_ld_wait();
-        if (valid < 64) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (c * 32 + e >= valid) sr[e] = __float_as_uint(-INFINITY);
-        }
-        uint32_t pw[8];
-#pragma unroll
-        for (int w = 0; w < 8; ++w) {
-          const uint32_t e0 = exp2_pair(__uint_as_float(sr[4 * w]), __uint_as_float(sr[4 * w + 1]), scale2, nbias2);
-          const uint32_t e1 = exp2_pair(__uint_as_float(sr[4 * w + 2]), __uint_as_float(sr[4 * w + 3]), scale2, nbias2);
-          hs0 = hadd2(hs0, e0);
-          hs1 = hadd2(hs1, e1);
-          pw[w] = e4m3x4_f16(e0, e1);
-        }
-        tmem_st8(s_col + hf * 64 + c * 8, pw);
+      for (int w = 0; w < 8; ++w) {
+        const uint32_t e0 = exp2_pair(__uint_as_float(sr[4 * w]), __uint_as_float(sr[4 * w + 1]), scale2, nbias2);
+        const uint32_t e1 = exp2_pair(__uint_as_float(sr[4 * w + 2]), __uint_as_float(sr[4 * w + 3]), scale2, nbias2);
+        hs0 = hadd2(hs0, e0);
+        hs1 = hadd2(hs1, e1);
+        pw[w] = e4m3x4_f16(e0, e1);
       }
+      tmem_st8(s_col, pw);
       l += hsum2_f32(hadd2(hs0, hs1));
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full[i]);
+      mbar_arrive(&p_full[b]);
     }
-    // ---- epilogue: row sum of both halves, then this half's 64 columns of O / l * vscale -> bf16
-    lx[(i * 2 + hf) * 128 + r] = l;
-    asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
-    const float lt = l + lx[(i * 2 + (hf ^ 1)) * 128 + r];
+    // ---- epilogue: row sum over the four warps, then this warp's 32 columns of O / l * vscale -> bf16
+    lx[kq * 128 + r] = l;
+    asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
+    const float lt = (lx[r] + lx[128 + r]) + (lx[256 + r] + lx[384 + r]);
     ok = ok && mbar_wait(o_done, 0, 212);
     ok = __all_sync(0xffffffffu, ok);
     if (ok) {
       tc_fence_after();
       const float inv_l = 1.0f / lt;
-      const float* vs = p.vscale + h * 128 + hf * 64;
-      __nv_bfloat16* dst = p.out + (long long)query * p.ldo + h * 128 + hf * 64;
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t o[32];
-        __syncwarp();
-        tmem_ld32(o_col + c * 32, o);
-        tmem_ld_wait();
-        if (query < p.S) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+      const float* vs = p.vscale + h * 128 + kq * 32;
+      uint32_t o[32];
+      tmem_ld32(o_col, o);
+      tmem_ld_wait();
+      if (query < p.S) {
+        uint4* d4 = reinterpret_cast<uint4*>(p.out + (long long)query * p.ldo + h * 128 + kq * 32);
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            float f[8];
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float f[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(o[q4 * 8 + e]) * inv_l * vs[c * 32 + q4 * 8 + e];
-            d4[q4] = make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]), pack_bf16(f[4], f[5]),
-                                pack_bf16(f[6], f[7]));
-          }
+          for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(o[q4 * 8 + e]) * inv_l * vs[q4 * 8 + e];
+          d4[q4] = make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]), pack_bf16(f[4], f[5]),
+                              pack_bf16(f[6], f[7]));
         }
       }
     }

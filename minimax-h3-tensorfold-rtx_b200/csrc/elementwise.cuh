@@ -106,6 +106,7 @@ __global__ void __launch_bounds__(256) norm_mod_kernel(NormModArgs a) {
   if (a.codes) inv_g = __fdiv_rn(1.0f, a.slot->act);
   float amax = 0.f;
   const int kgroups = a.D >> 4;
+  const bool sf_words = (kgroups & 3) == 0;   // every 4-group quad lies inside the row
 #pragma unroll
   for (int it = 0; it < MAXIT; ++it) {
     int c = it * 256 + lane * 8;
@@ -150,11 +151,16 @@ __global__ void __launch_bounds__(256) norm_mod_kernel(NormModArgs a) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) xs[j] = __fmul_rn(xs[j], inv);
       uint32_t cw = e2m1x8(xs);
+      // the scales of groups 4b..4b+3 (lanes 8b, 8b+2, 8b+4, 8b+6) are 4 consecutive bytes in both layouts: one word
+      const uint32_t w1 = __shfl_down_sync(0xffffffffu, sfb, 2), w2 = __shfl_down_sync(0xffffffffu, sfb, 4),
+                     w3 = __shfl_down_sync(0xffffffffu, sfb, 6);
       if (ok) {
         *reinterpret_cast<uint32_t*>(a.codes + (size_t)row * (a.D >> 1) + (c >> 1)) = cw;
-        if ((lane & 1) == 0) {
-          int k16 = c >> 4;
-          size_t off = a.sf_tiled ? sf_tiled_offset(row, k16, kgroups) : (size_t)row * kgroups + k16;
+        const int k16 = c >> 4;
+        const size_t off = a.sf_tiled ? sf_tiled_offset(row, k16, kgroups) : (size_t)row * kgroups + k16;
+        if (sf_words) {
+          if ((lane & 7) == 0) *reinterpret_cast<uint32_t*>(a.sf + off) = sfb | (w1 << 8) | (w2 << 16) | (w3 << 24);
+        } else if ((lane & 1) == 0) {
           a.sf[off] = (uint8_t)sfb;
         }
       }
@@ -189,7 +195,10 @@ __global__ void __launch_bounds__(256) nvfp4_quant_kernel(QuantArgs a) {
   const int groups = a.K >> 4;
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   float am = 0.f;
-  if (gid < (long long)a.R * groups) {
+  uint32_t sfb = 0;
+  size_t off = 0;
+  const bool live = gid < (long long)a.R * groups;
+  if (live) {
     const int r = (int)(gid / groups), k16 = (int)(gid % groups);
     const int c = k16 * 16;
     const __nv_bfloat16* src = a.x + (long long)(c / a.cblk) * a.blk_stride + (long long)r * a.ldx + (c % a.cblk);
@@ -204,9 +213,17 @@ __global__ void __launch_bounds__(256) nvfp4_quant_kernel(QuantArgs a) {
     }
     const float g = a.g_ptr ? *a.g_ptr : a.g;
     uint32_t cw[2];
-    uint32_t sfb = quant_group16(v, __fdiv_rn(1.0f, g), cw);
+    sfb = quant_group16(v, __fdiv_rn(1.0f, g), cw);
     *reinterpret_cast<uint2*>(a.codes + (size_t)r * (a.K >> 1) + (c >> 1)) = make_uint2(cw[0], cw[1]);
-    a.sf[a.sf_tiled ? sf_tiled_offset(r, k16, groups) : (size_t)r * groups + k16] = (uint8_t)sfb;
+    off = a.sf_tiled ? sf_tiled_offset(r, k16, groups) : (size_t)r * groups + k16;
+    if ((groups & 3) != 0) a.sf[off] = (uint8_t)sfb;
+  }
+  // with groups % 4 == 0, lanes 4b..4b+3 hold the scales of 4 consecutive groups of one row: one word store
+  if ((groups & 3) == 0) {
+    const uint32_t w1 = __shfl_down_sync(0xffffffffu, sfb, 1), w2 = __shfl_down_sync(0xffffffffu, sfb, 2),
+                   w3 = __shfl_down_sync(0xffffffffu, sfb, 3);
+    if (live && (threadIdx.x & 3) == 0)
+      *reinterpret_cast<uint32_t*>(a.sf + off) = sfb | (w1 << 8) | (w2 << 16) | (w3 << 24);
   }
   if (a.amax) {
     am = warp_max(am);

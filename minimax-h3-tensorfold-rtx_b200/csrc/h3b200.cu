@@ -134,7 +134,7 @@ struct AttnWs {
 
 AttnWs attn_ws(int S, int H) {
   AttnWs w;
-  w.SP = (S + 255) / 256 * 256;
+  w.SP = (S + 127) / 128 * 128;
   w.nblk = (S + 127) / 128;
   size_t o = 0;
   auto take = [&](size_t bytes) {
@@ -350,8 +350,7 @@ int h3_qknorm_rope(void* q, void* k, long long ld, int S, int H, int rot, const 
     return fail(H3_ERR_ARG, "h3_qknorm_rope: misaligned pointer");
   QkNormArgs a{reinterpret_cast<__nv_bfloat16*>(q), reinterpret_cast<__nv_bfloat16*>(k), ld, S, H, rot, qw, kw, rope,
                eps};
-  long long rows = (long long)S * 2 * H;
-  qknorm_rope_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, S_(stream)>>>(a);
+  qknorm_rope_kernel<<<(unsigned)((S + 7) / 8), 256, 0, S_(stream)>>>(a);
   return check_launch("h3_qknorm_rope");
 }
 
@@ -397,7 +396,7 @@ int h3_attn_fp8(const void* q, const void* k, const void* v, long long ld, long 
   if ((rc = make_map_u8(&tv, vt8, w.SP, (uint64_t)H * 128, w.SP, 128, 128, "h3_attn_fp8(V)"))) return rc;
   if ((rc = smem_optin(attn_fp8_kernel, AttnSmem::TOTAL, &g_optin_attn, "h3_attn_fp8"))) return rc;
   AttnArgs p{qscale, kscale, vscale, reinterpret_cast<__nv_bfloat16*>(out), ldo, S, w.SP, H};
-  attn_fp8_kernel<<<dim3(w.SP / 256, H), kAttnThreads, AttnSmem::TOTAL, st>>>(tq, tk, tv, p);
+  attn_fp8_kernel<<<dim3(w.SP / kQTile, H), kAttnThreads, AttnSmem::TOTAL, st>>>(tq, tk, tv, p);
   return check_launch("h3_attn_fp8");
 }
 
