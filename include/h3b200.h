@@ -133,6 +133,18 @@ size_t h3_attn_workspace_bytes(int S, int H);
 int h3_attn_fp8(const void* q, const void* k, const void* v, long long ld, long long hstride, int S, int H, void* out,
                 long long ldo, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same attention as h3_attn_fp8 for callers that cannot allocate device memory -- for example code running
+ * inside a host framework that owns every device allocation (ComfyUI records and replays a block's allocations under
+ * its dynamic-VRAM mode), or a plugin handed only input and output buffers.  Its scratch is a fixed 64 MiB device
+ * array inside this library, held by every GPU that loads the library until the process exits; problems whose
+ * h3_attn_workspace_bytes(S, H) exceed 64 MiB - 1 KiB (about S * H <= 170,000, e.g. S = 4096 at H = 40) are
+ * rejected with H3_ERR_SHAPE.  The first call on a device looks up the array's device address (make it before any
+ * stream capture).  All calls share the array, so calls that overlap on the GPU (other streams, other threads) race;
+ * nothing in it needs to start at zero.  It allocates nothing.  This entry point has no counterpart in the
+ * reference. */
+int h3_attn_fp8_noalloc(const void* q, const void* k, const void* v, long long ld, long long hstride, int S, int H,
+                        void* out, long long ldo, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

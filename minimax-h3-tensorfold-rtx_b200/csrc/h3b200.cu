@@ -401,3 +401,54 @@ int h3_attn_fp8(const void* q, const void* k, const void* v, long long ld, long 
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------ no-alloc attention
+// Scratch of h3_attn_fp8_noalloc: one file-scope device array of kNoAllocScratchBytes.  Every GPU that loads this
+// library holds it until the process exits.  Host code must not pass the symbol itself to a kernel (on the host it
+// names a stand-in, not device memory): its device address comes from cudaGetSymbolAddress, looked up once per
+// device with that device current.
+constexpr size_t kNoAllocScratchBytes = 64ull << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(H3_ERR_CUDA, "h3_attn_fp8_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(H3_ERR_ARG, "h3_attn_fp8_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(H3_ERR_CUDA, "h3_attn_fp8_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return H3_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int h3_attn_fp8_noalloc(const void* q, const void* k, const void* v, long long ld, long long hstride, int S, int H,
+                        void* out, long long ldo, void* stream) {
+  if (S <= 0 || H <= 0) return fail(H3_ERR_SHAPE, "h3_attn_fp8_noalloc: S and H must be positive");
+  const size_t need = h3_attn_workspace_bytes(S, H);
+  if (need + 1024 > kNoAllocScratchBytes)
+    return fail(H3_ERR_SHAPE,
+                "h3_attn_fp8_noalloc: S=%d, H=%d needs %zu bytes of scratch, beyond the fixed %zu-byte array; use "
+                "h3_attn_fp8 with a caller-provided workspace",
+                S, H, need, kNoAllocScratchBytes - 1024);
+  void* base = nullptr;
+  int rc = noalloc_scratch(&base);
+  if (rc) return rc;
+  // the workspace layout wants a 1024-byte aligned start; the array is 256-aligned, so step to the next 1024
+  uint8_t* ws = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(base) + 1023) & ~uintptr_t(1023));
+  return h3_attn_fp8(q, k, v, ld, hstride, S, H, out, ldo, ws, kNoAllocScratchBytes - 1024, stream);
+}
+
+}  // extern "C"

@@ -46,6 +46,7 @@ _SIGS = {
     "h3_qknorm_rope": [vp, vp, i64, i32, i32, i32, vp, vp, vp, f32, vp],
     "h3_attn_workspace_bytes": ([i32, i32], sz),
     "h3_attn_fp8": [vp, vp, vp, i64, i64, i32, i32, vp, i64, vp, sz, vp],
+    "h3_attn_fp8_noalloc": [vp, vp, vp, i64, i64, i32, i32, vp, i64, vp],
 }
 
 _lib = None
