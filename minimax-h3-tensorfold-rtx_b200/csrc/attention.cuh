@@ -379,7 +379,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&p_full[b], 512);
+      mbar_init(&p_full[b], 16);   // one arrival per softmax warp
     }
     mbar_init(pv_done, 1);
     mbar_init(o_done, 1);
@@ -549,7 +549,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       l += hsum2_f32(hadd2(hs0, hs1));
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full[b]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[b]);
     }
     // ---- epilogue: row sum over the four warps, then this warp's 32 columns of O / l * vscale -> bf16
     lx[kq * 128 + r] = l;

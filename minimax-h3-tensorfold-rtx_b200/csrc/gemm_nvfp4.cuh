@@ -6,8 +6,8 @@
 // (tfvideo/kernels.py:66-84, tfvideo/linear.py:219-233).
 //
 // CTA tile 128 x BN (BN = 256 or 128), K tile 256 elements (128 bytes, one 128-byte swizzle row), 4-stage smem ring.
-// Warp 0: TMA producer.  Warp 1: TMEM owner and MMA issuer (one thread).  Warps 2-5: epilogue, warp w reading TMEM
-// lanes 32 * (w % 4) .. +31, i.e. one output row per thread.  Persistent over output tiles.
+// Warp 0: TMA producer.  Warp 1: TMEM owner and MMA issuer (one thread).  Warps 2-9: epilogue, warp w reading TMEM
+// lanes 32 * (w % 4) .. +31 (one output row per thread) and half (w - 2) / 4 of the columns.  Persistent over tiles.
 #pragma once
 
 #include "common.cuh"
@@ -37,7 +37,7 @@ struct GemmArgs {
 };
 
 constexpr int kGemmStages = 4;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue (two per TMEM lane quadrant)
 
 template <int BN>
 struct GemmSmem {
@@ -114,7 +114,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 4);
+    mbar_init(acc_empty, 8);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -191,6 +191,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;
+    const int cofs = ((warp - 2) >> 2) * (BN / 2);   // this warp's half of the tile's columns
     const float alpha = p.a_slot->act * p.g_b;
     const float inv_q = EPI == H3_EPI_ACT_Q ? __fdiv_rn(1.0f, p.q_slot->act) : 0.f;
     const int F = p.act_kind ? (p.N >> 1) : p.N;   // activation width (ACT_*)
@@ -204,27 +205,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const float* __restrict__ gate = nullptr;
       if (EPI == H3_EPI_GATE_RESID && live) {
         // pull this row's slice of the residual into L2 while the tile's MMAs run
-        xrow = p.x + (size_t)row * p.ldx + n0;
-        gate = p.mod + ((size_t)p.idx[row] * 6 + 3 * p.gate_part + 2) * p.N + n0;
+        xrow = p.x + (size_t)row * p.ldx + n0 + cofs;
+        gate = p.mod + ((size_t)p.idx[row] * 6 + 3 * p.gate_part + 2) * p.N + n0 + cofs;
 #pragma unroll
-        for (int b = 0; b < BN * 2; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"((const char*)xrow + b));
+        for (int b = 0; b < BN; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"((const char*)xrow + b));
       }
       const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, ti & 1, 103));   // tcgen05.ld is warp-wide
       if (!ok) break;
       tc_fence_after();
       // phase 1: accumulator -> bf16(acc * gA * gB + bias) in registers, then TMEM goes back to the MMA warp
-      uint32_t hold[BN / 2];
+      uint32_t hold[BN / 4];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = 0; c < BN / 64; ++c) {
         uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, r);
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + cofs + c * 32, r);
         tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           float v0 = __uint_as_float(r[2 * j]) * alpha, v1 = __uint_as_float(r[2 * j + 1]) * alpha;
           if (p.bias) {
-            v0 += p.bias[n0 + c * 32 + 2 * j];
-            v1 += p.bias[n0 + c * 32 + 2 * j + 1];
+            v0 += p.bias[n0 + cofs + c * 32 + 2 * j];
+            v1 += p.bias[n0 + cofs + c * 32 + 2 * j + 1];
           }
           hold[c * 16 + j] = pack_bf16(v0, v1);
         }
@@ -235,8 +236,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!live) continue;
       // phase 2: the global-memory half, overlapping the next tile's mainloop
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int nc = n0 + c * 32;
+      for (int c = 0; c < BN / 64; ++c) {
+        const int nc = n0 + cofs + c * 32;
         uint32_t y[16];   // 32 bf16 values, columns nc..nc+31
         chunk_words(hold, c, y);
         if (EPI == H3_EPI_STORE) {
