@@ -129,7 +129,8 @@ size_t h3_attn_workspace_bytes(int S, int H);
 /* Non-causal FP8 attention softmax(q k^T / sqrt(128)) v over H heads of head_dim 128 (replaces the attention
  * backends of tfvideo/attention.py:44-54 and fp4attn.attention(qk="fp8", pv="fp8"), tfvideo/fp4attn.py:245-290).
  * Element (t, h, d) of q / k / v at base + t * ld + h * hstride + d (bf16); out (t, h, d) at out + t * ldo + h * 128
- * + d (bf16).  workspace: h3_attn_workspace_bytes(S, H) bytes, 1024-byte aligned. */
+ * + d (bf16).  workspace: h3_attn_workspace_bytes(S, H) bytes, 1024-byte aligned.  S <= 262,144 and H <= 65,535
+ * (H3_ERR_SHAPE beyond). */
 int h3_attn_fp8(const void* q, const void* k, const void* v, long long ld, long long hstride, int S, int H, void* out,
                 long long ldo, void* workspace, size_t workspace_bytes, void* stream);
 

@@ -279,24 +279,28 @@ struct AttnArgs {
 };
 
 constexpr int kAttnStages = 4;
-// One 128-row query tile per CTA with two S buffers in TMEM, so QK^T of KV tile j + 1 runs on the tensor cores while
-// the softmax of tile j does.  Warps 0-15: softmax, warp w on TMEM lane quadrant w % 4 and keys 32 (w / 4) .. +31 of
-// each KV tile (four warps share each row: an FP8 tile leaves the softmax about half the MMA time a bf16 tile does);
-// warp 16: TMA; warp 17: MMA.
-constexpr int kAttnThreads = 576;
-constexpr int kProdWarp = 16, kMmaWarp = 17;
+// One CTA = two 128-row query tiles (A, B) of one head, ping-ponged on the tensor cores: while the softmax of one
+// tile runs, the PV and next QK^T of the other do.  Warps 0-3: softmax of tile A, warps 4-7: tile B -- warp w on TMEM
+// lane quadrant w % 4, one thread per query row holding the row's whole 128-key S tile in registers, so the row max
+// needs no exchange between threads; warp 8: TMA; warp 9: MMA.  TMEM columns: S_A [0, 128), S_B [128, 256),
+// O_A [256, 384), O_B [384, 512); P of keys 32c..32c+31 (e4m3) is written over S columns 32c..32c+7 of its tile.
+constexpr int kAttnThreads = 320;
+constexpr int kProdWarp = 8, kMmaWarp = 9;
 constexpr int kQTile = 128;
+constexpr int kQPerCta = 2 * kQTile;
 constexpr float kTau = 2.0f;        // running-max lag allowed before O is rescaled (log2 units)
 constexpr float kPOffset = 8.807354922057604f - kTau;   // log2(448) - tau
+// Pairs of each 32-key chunk whose exp2 runs as a polynomial on the FMA pipe instead of the MUFU (bit i: keys 2i,
+// 2i + 1).  The MUFU issues one ex2 per 8 lanes per cycle per SM sub-partition, which bounds an FP8 tile's softmax
+// at about twice the tile's MMA time; moving part of the exponentials to the FMA pipe shortens it.
+constexpr uint32_t kPolyPairs = 0x5252u;
 struct AttnSmem {
   static constexpr int TILE = 128 * 128;
-  static constexpr int Q_OFF = 0;
-  static constexpr int KV_OFF = TILE;                   // per stage: K, V^T
-  static constexpr int KSC_OFF = KV_OFF + kAttnStages * 2 * TILE;   // this head's K-block scales
-  static constexpr int MAX_KBLK = 2048;                                // sequences up to 262,144 tokens
-  static constexpr int XCH_OFF = KSC_OFF + MAX_KBLK * 4;          // row-max exchange [2 parities][4 warps][128]
-  static constexpr int LX_OFF = XCH_OFF + 2 * 4 * 128 * 4;         // row-sum exchange [4 warps][128]
-  static constexpr int BAR_OFF = LX_OFF + 4 * 128 * 4;
+  static constexpr int Q_OFF = 0;                                      // Q tiles A, B
+  static constexpr int KV_OFF = 2 * TILE;                               // per stage: K, V^T
+  static constexpr int KSC_OFF = KV_OFF + kAttnStages * 2 * TILE;       // this head's K-block scales
+  static constexpr int MAX_KBLK = 2048;                                 // sequences up to 262,144 tokens
+  static constexpr int BAR_OFF = KSC_OFF + MAX_KBLK * 4;
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;
 };
 
@@ -310,40 +314,92 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
   return m;
 }
-// (exp2(a * scale - bias), exp2(b * scale - bias)) as f16x2 (a in the low half): one packed fp32 FMA, one packed
-// conversion and one MUFU ex2 for two probabilities.  P is rounded to e4m3 next, so f16 precision is ample.
-__device__ __forceinline__ uint32_t exp2_pair(float a, float b, uint64_t scale2, uint64_t nbias2) {
-  uint32_t h;
-  asm("{\n\t.reg .b64 x, y;\n\t.reg .f32 y0, y1;\n\t.reg .b32 hh;\n\t"
-      "mov.b64 x, {%1, %2};\n\t"
-      "fma.rn.f32x2 y, x, %3, %4;\n\t"
-      "mov.b64 {y0, y1}, y;\n\t"
-      "cvt.rn.f16x2.f32 hh, y1, y0;\n\t"
-      "ex2.approx.f16x2 %0, hh;\n\t}"
-      : "=r"(h)
-      : "f"(a), "f"(b), "l"(scale2), "l"(nbias2));
-  return h;
-}
 __device__ __forceinline__ uint64_t f32x2_splat(float v) {
   uint64_t r;
   asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(v));
   return r;
 }
-__device__ __forceinline__ uint32_t hadd2(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+__device__ __forceinline__ uint64_t f32x2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
   return r;
 }
-__device__ __forceinline__ float hsum2_f32(uint32_t h) {
-  __half2 v = *reinterpret_cast<__half2*>(&h);
-  return __low2float(v) + __high2float(v);
+__device__ __forceinline__ void f32x2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
 }
-// two f16x2 pairs -> four e4m3 bytes (lo pair's low half in byte 0)
-__device__ __forceinline__ uint32_t e4m3x4_f16(uint32_t lo, uint32_t hi) {
-  uint16_t a, b;
-  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(a) : "r"(lo));
-  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(b) : "r"(hi));
-  return (uint32_t)a | ((uint32_t)b << 16);
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// 2^x for a pair, by range reduction x = n + g (n = round(x), |g| <= 1/2) and a degree-3 polynomial for 2^g (a
+// relative-error least-squares fit on [-1/2, 1/2]; max relative error 7.5e-5, below the e4m3 rounding P gets next
+// by three orders of magnitude).  n comes from the magic-number rounding x + (1.5 * 2^23 + 127): the sum's low
+// mantissa bits hold 127 + n, which shifted into the exponent field is the fp32 2^n.  x is clamped to >= -126.
+__device__ __forceinline__ uint64_t exp2_poly_pair(uint64_t x2) {
+  constexpr float kMagic = 12582912.0f + 127.0f;
+  float a, b;
+  f32x2_unpack(x2, a, b);
+  const uint64_t x = f32x2_pack(fmaxf(a, -126.0f), fmaxf(b, -126.0f));
+  const uint64_t t = add2(x, f32x2_splat(kMagic));
+  const uint64_t n = add2(t, f32x2_splat(-kMagic));
+  const uint64_t g = fma2(n, f32x2_splat(-1.0f), x);
+  uint64_t p = fma2(f32x2_splat(0.0551716685295105f), g, f32x2_splat(0.2426111400127411f));
+  p = fma2(p, g, f32x2_splat(0.6932609677314758f));
+  p = fma2(p, g, f32x2_splat(0.9999280571937561f));
+  float t0, t1;
+  f32x2_unpack(t, t0, t1);
+  return mul2(p, f32x2_pack(__uint_as_float(__float_as_uint(t0) << 23), __uint_as_float(__float_as_uint(t1) << 23)));
+}
+__device__ __forceinline__ uint64_t exp2_mufu_pair(uint64_t x2) {
+  float a, b;
+  f32x2_unpack(x2, a, b);
+  return f32x2_pack(ex2(a), ex2(b));
+}
+// 32 scores of one row -> 8 words of e4m3 P = exp2(s * scale - bias) (key 4w + i in byte i of word w); l2 += the
+// unrounded P (two fp32 lanes).
+__device__ __forceinline__ void p_chunk(const uint32_t (&s)[32], uint64_t scale2, uint64_t nbias2, uint32_t (&pw)[8],
+                                        uint64_t& l2a, uint64_t& l2b) {
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    uint64_t y[2];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int pi = 2 * w + hh;
+      const uint64_t x = fma2(f32x2_pack(__uint_as_float(s[2 * pi]), __uint_as_float(s[2 * pi + 1])), scale2, nbias2);
+      y[hh] = ((kPolyPairs >> pi) & 1u) ? exp2_poly_pair(x) : exp2_mufu_pair(x);
+    }
+    l2a = add2(l2a, y[0]);
+    l2b = add2(l2b, y[1]);
+    float a, b, c, d;
+    f32x2_unpack(y[0], a, b);
+    f32x2_unpack(y[1], c, d);
+    pw[w] = e4m3x2(a, b) | (e4m3x2(c, d) << 16);
+  }
+}
+__device__ __forceinline__ float max_chunk(const uint32_t (&s)[32], float m) {
+  float a = m, b = m;
+#pragma unroll
+  for (int e = 0; e < 32; e += 4) {
+    a = max3(a, __uint_as_float(s[e]), __uint_as_float(s[e + 1]));
+    b = max3(b, __uint_as_float(s[e + 2]), __uint_as_float(s[e + 3]));
+  }
+  return fmaxf(a, b);
+}
+__device__ __forceinline__ void mask_chunk(uint32_t (&s)[32], int valid) {
+#pragma unroll
+  for (int e = 0; e < 32; ++e)
+    if (e >= valid) s[e] = __float_as_uint(-INFINITY);
 }
 
 __global__ void __launch_bounds__(kAttnThreads, 1)
@@ -357,15 +413,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = k_full + kAttnStages;
   uint64_t* kv_empty = v_full + kAttnStages;
-  uint64_t* s_full = kv_empty + kAttnStages;   // [2]: QK^T of tile j in S buffer j % 2
-  uint64_t* p_full = s_full + 2;               // [2]: P of tile j written over S buffer j % 2
-  uint64_t* pv_done = p_full + 2;              // one phase per PV of a tile
-  uint64_t* o_done = pv_done + 1;
+  uint64_t* s_full = kv_empty + kAttnStages;   // [tile]: QK^T of the tile's current KV tile (and all earlier MMAs) done
+  uint64_t* p_full = s_full + 2;               // [tile]: P written over S by the tile's four softmax warps
+  uint64_t* o_done = p_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y;
-  const int q0 = blockIdx.x * kQTile;
+  const int q0 = blockIdx.x * kQPerCta;
+  const bool has_b = q0 + kQTile < p.S;       // tile B holds queries of this sequence
   const int nkv = (p.S + 127) / 128;
   float* ksc_s = reinterpret_cast<float*>(smem + L::KSC_OFF);
   for (int i = threadIdx.x; i < nkv; i += blockDim.x) ksc_s[i] = p.kscale[(size_t)h * (p.SP / 128) + i];
@@ -377,11 +433,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&p_full[b], 16);   // one arrival per softmax warp
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);   // one arrival per softmax warp of the tile
     }
-    mbar_init(pv_done, 1);
     mbar_init(o_done, 1);
     fence_barrier_init();
   }
@@ -393,16 +448,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: S buffer 0 [0, 128), S buffer 1 [128, 256), O [256, 384).  P of keys 32k..32k+31 goes to columns
-  // 32k..32k+7 of its S buffer (the columns the warp owning those keys read).
 
   if (warp == kProdWarp) {
     if (lane == 0) {
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
-      mbar_arrive_expect_tx(q_full, L::TILE);
+      mbar_arrive_expect_tx(q_full, has_b ? 2 * L::TILE : L::TILE);
       tma_load_2d(smem + L::Q_OFF, &tmQ, 0, h * p.SP + q0, q_full);
+      if (has_b) tma_load_2d(smem + L::Q_OFF + L::TILE, &tmQ, 0, h * p.SP + q0 + kQTile, q_full);
       for (int j = 0; j < nkv; ++j) {
         const int st = j % kAttnStages;
         const uint32_t ph = (j / kAttnStages) & 1;
@@ -418,162 +472,157 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_fp8(128, 128);
       const uint32_t qs = smem_u32(smem + L::Q_OFF);
-      auto issue_s = [&](int b, int st) {
+      auto issue_s = [&](int t, int st) {   // S_t = Q_t K^T
         const uint32_t ks = smem_u32(smem + L::KV_OFF + st * 2 * L::TILE);
+        const uint32_t qt = qs + t * L::TILE;
 #pragma unroll
         for (int kb = 0; kb < 4; ++kb)
-          mma_fp8_ss(tmem + b * 128, sdesc_kmajor_sw128(qs + kb * 32), sdesc_kmajor_sw128(ks + kb * 32), idesc, kb != 0);
+          mma_fp8_ss(tmem + t * 128, sdesc_kmajor_sw128(qt + kb * 32), sdesc_kmajor_sw128(ks + kb * 32), idesc, kb != 0);
       };
-      auto issue_pv = [&](int b, int st, int j) {
+      auto issue_pv = [&](int t, int st, int j) {   // O_t += P_t V
         const uint32_t vs = smem_u32(smem + L::KV_OFF + st * 2 * L::TILE + L::TILE);
 #pragma unroll
         for (int kb = 0; kb < 4; ++kb)
-          mma_fp8_ts(tmem + 256, tmem + b * 128 + kb * 32, sdesc_kmajor_sw128(vs + kb * 32), idesc, (j | kb) != 0);
+          mma_fp8_ts(tmem + 256 + t * 128, tmem + t * 128 + kb * 32, sdesc_kmajor_sw128(vs + kb * 32), idesc,
+                     (j | kb) != 0);
       };
-      bool ok = mbar_wait(q_full, 0, 202);
-      for (int j = 0; ok && j < 2 && j < nkv; ++j) {   // prologue: S of tiles 0 and 1
-        if (!(ok = mbar_wait(&k_full[j], 0, 203))) break;
+      bool ok = mbar_wait(q_full, 0, 202) && mbar_wait(&k_full[0], 0, 203);
+      if (ok) {
         tc_fence_after();
-        issue_s(j, j);
-        tc_commit(&s_full[j]);
+        issue_s(0, 0);
+        tc_commit(&s_full[0]);
+        if (has_b) {
+          issue_s(1, 0);
+          tc_commit(&s_full[1]);
+        }
       }
       for (int j = 0; ok && j < nkv; ++j) {
-        const int b = j & 1, st = j % kAttnStages;
-        if (!(ok = mbar_wait(&p_full[b], (j >> 1) & 1, 204) && mbar_wait(&v_full[st], (j / kAttnStages) & 1, 205)))
-          break;
+        const int st = j % kAttnStages;
+        const bool next = j + 1 < nkv;
+        const int st1 = (j + 1) % kAttnStages;
+        if (!(ok = mbar_wait(&p_full[0], j & 1, 204) && mbar_wait(&v_full[st], (j / kAttnStages) & 1, 205))) break;
         tc_fence_after();
-        issue_pv(b, st, j);
-        tc_commit(pv_done);
-        tc_commit(&kv_empty[st]);
-        if (j + 2 < nkv) {
-          const int st2 = (j + 2) % kAttnStages;
-          if (!(ok = mbar_wait(&k_full[st2], ((j + 2) / kAttnStages) & 1, 206))) break;
+        issue_pv(0, st, j);
+        if (!has_b) tc_commit(&kv_empty[st]);
+        if (next) {
+          if (!(ok = mbar_wait(&k_full[st1], ((j + 1) / kAttnStages) & 1, 206))) break;
           tc_fence_after();
-          issue_s(b, st2);   // after PV(j) in issue order, so P(j) is consumed before S(j + 2) overwrites it
-          tc_commit(&s_full[b]);
+          issue_s(0, st1);   // after PV_A(j) in issue order, so P_A(j) is consumed before S_A(j + 1) overwrites it
+          tc_commit(&s_full[0]);
+        }
+        if (has_b) {
+          if (!(ok = mbar_wait(&p_full[1], j & 1, 207))) break;
+          tc_fence_after();
+          issue_pv(1, st, j);
+          tc_commit(&kv_empty[st]);
+          if (next) {
+            issue_s(1, st1);
+            tc_commit(&s_full[1]);
+          }
         }
       }
       tc_commit(o_done);
     }
   } else {
-    // ------------------------------------------------------------------ softmax warps
-    const int kq = warp >> 2;        // keys 32 kq .. 32 kq + 31 of each tile, O columns 32 kq .. 32 kq + 31
-    const int qd = warp & 3;         // TMEM lane quadrant
+    // ------------------------------------------------------------------ softmax: one thread per query row
+    const int t = warp >> 2;          // query tile
+    const int qd = warp & 3;          // TMEM lane quadrant
     const int r = qd * 32 + lane;
-    const int query = q0 + r;
+    const int query = q0 + t * kQTile + r;
     const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
-    const uint32_t o_col = tmem + lane_off + 256 + kq * 32;
-    const int bar_id = 1 + qd;       // named barrier of the four warps sharing these rows
-    float* xch = reinterpret_cast<float*>(smem + L::XCH_OFF);
-    float* lx = reinterpret_cast<float*>(smem + L::LX_OFF);
-    const float qr = p.qscale[(size_t)h * p.SP + query];
-    float m_used = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
-      const int b = j & 1;
-      const uint32_t s_col = tmem + lane_off + b * 128 + kq * 32;
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[b], (j >> 1) & 1, 210));
-      const float scale = qr * ksc_s[j];
-      const int valid = p.S - j * 128 - kq * 32;   // keys of this warp's slice inside the sequence
-      uint32_t sr[32];
-      float mloc = -INFINITY;
-      if (ok) {
-        tc_fence_after();
-        tmem_ld32(s_col, sr);
-        tmem_ld_wait();
-        if (valid < 32) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (e >= valid) sr[e] = __float_as_uint(-INFINITY);
-        }
-        float m[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint32_t* f = sr + 8 * k;
-          m[k] = max3(max3(__uint_as_float(f[0]), __uint_as_float(f[1]), __uint_as_float(f[2])),
-                      max3(__uint_as_float(f[3]), __uint_as_float(f[4]), __uint_as_float(f[5])),
-                      fmaxf(__uint_as_float(f[6]), __uint_as_float(f[7])));
-        }
-        mloc = fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
-      }
-      float* xs = xch + (j & 1) * 512;
-      xs[kq * 128 + r] = mloc;
-      // exchange the four partial maxima; the barrier also ANDs the warps' wait results, so the four warps sharing
-      // these rows leave the loop together (a named barrier has no timeout)
-      {
-        uint32_t all;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred p, %2, 128, p;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(all)
-            : "r"((uint32_t)ok), "r"(bar_id)
-            : "memory");
-        ok = all != 0;
-      }
+    const uint32_t s_col = tmem + lane_off + t * 128;
+    const uint32_t o_col = tmem + lane_off + 256 + t * 128;
+    bool ok = t == 0 || has_b;
+    const bool live = ok;
+    const float qr = live ? p.qscale[(size_t)h * p.SP + query] : 0.f;
+    float m_used = -INFINITY;
+    uint64_t l2a = 0, l2b = 0;
+    for (int j = 0; live && j < nkv; ++j) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, 210));
       if (!ok) break;
-      const float mx = fmaxf(fmaxf(xs[r], xs[128 + r]), fmaxf(xs[256 + r], xs[384 + r]));
+      tc_fence_after();
+      uint32_t s0[32], s1[32], s2[32], s3[32];
+      tmem_ld32(s_col, s0);
+      tmem_ld32(s_col + 32, s1);
+      tmem_ld32(s_col + 64, s2);
+      tmem_ld32(s_col + 96, s3);
+      tmem_ld_wait();
+      const int valid = p.S - j * 128;   // keys of this KV tile inside the sequence (only the last is ragged)
+      if (valid < 128) {
+        mask_chunk(s0, valid);
+        mask_chunk(s1, valid - 32);
+        mask_chunk(s2, valid - 64);
+        mask_chunk(s3, valid - 96);
+      }
+      const float mx = fmaxf(fmaxf(max_chunk(s0, -INFINITY), max_chunk(s1, -INFINITY)),
+                             fmaxf(max_chunk(s2, -INFINITY), max_chunk(s3, -INFINITY)));
+      const float scale = qr * ksc_s[j];
       const float mnew = mx * scale;
-      // raise the running max only when a row's max grew by more than tau; the tcgen05 ld/st of O are warp-wide,
-      // so a warp rescales when any of its rows must (the others multiply by 1); each warp rescales its 32 columns
-      // once the previous tile's PV has landed
+      // raise the running max only when the row's max grew by more than tau (then O and l are rescaled)
       const bool need = mnew > m_used + kTau;
       float alpha = 1.0f;
-      if (need && j > 0) alpha = ex2(m_used - mnew);
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // a wait that gives up has recorded the error; the warp stays in step with its partners
-        __all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, 213));
-        tc_fence_after();
-        uint32_t o[32];
-        tmem_ld32(o_col, o);
-        tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-        tmem_st32(o_col, o);
-      }
       if (need) {
-        l *= alpha;
+        alpha = ex2(m_used - mnew);
         m_used = mnew;
+        const uint64_t a2 = f32x2_splat(alpha);
+        l2a = mul2(l2a, a2);
+        l2b = mul2(l2b, a2);
       }
       const uint64_t scale2 = f32x2_splat(scale), nbias2 = f32x2_splat(kPOffset - m_used);
       uint32_t pw[8];
-      uint32_t hs0 = 0, hs1 = 0;
-#pragma unroll
-      for (int w = 0; w < 8; ++w) {
-        const uint32_t e0 = exp2_pair(__uint_as_float(sr[4 * w]), __uint_as_float(sr[4 * w + 1]), scale2, nbias2);
-        const uint32_t e1 = exp2_pair(__uint_as_float(sr[4 * w + 2]), __uint_as_float(sr[4 * w + 3]), scale2, nbias2);
-        hs0 = hadd2(hs0, e0);
-        hs1 = hadd2(hs1, e1);
-        pw[w] = e4m3x4_f16(e0, e1);
-      }
+      p_chunk(s0, scale2, nbias2, pw, l2a, l2b);
       tmem_st8(s_col, pw);
-      l += hsum2_f32(hadd2(hs0, hs1));
+      p_chunk(s1, scale2, nbias2, pw, l2a, l2b);
+      tmem_st8(s_col + 32, pw);
+      p_chunk(s2, scale2, nbias2, pw, l2a, l2b);
+      tmem_st8(s_col + 64, pw);
+      p_chunk(s3, scale2, nbias2, pw, l2a, l2b);
+      tmem_st8(s_col + 96, pw);
+      // O holds PV of tiles < j (s_full also tracks PV(j - 1)); the tcgen05 ld/st are warp-wide, so a warp rescales
+      // when any of its rows must (the others multiply by 1)
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_col + 32 * c, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(o_col + 32 * c, o);
+        }
+      }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[b]);
+      if (lane == 0) mbar_arrive(&p_full[t]);
     }
-    // ---- epilogue: row sum over the four warps, then this warp's 32 columns of O / l * vscale -> bf16
-    lx[kq * 128 + r] = l;
-    asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
-    const float lt = (lx[r] + lx[128 + r]) + (lx[256 + r] + lx[384 + r]);
-    ok = ok && mbar_wait(o_done, 0, 212);
-    ok = __all_sync(0xffffffffu, ok);
-    if (ok) {
+    // ---- epilogue: O / l * vscale -> bf16, this thread's row
+    if (live) {
+      ok = ok && mbar_wait(o_done, 0, 212);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (live && ok) {
       tc_fence_after();
-      const float inv_l = 1.0f / lt;
-      const float* vs = p.vscale + h * 128 + kq * 32;
-      uint32_t o[32];
-      tmem_ld32(o_col, o);
-      tmem_ld_wait();
-      if (query < p.S) {
-        uint4* d4 = reinterpret_cast<uint4*>(p.out + (long long)query * p.ldo + h * 128 + kq * 32);
+      float la, lb, lc, ld;
+      f32x2_unpack(l2a, la, lb);
+      f32x2_unpack(l2b, lc, ld);
+      const float inv_l = 1.0f / ((la + lb) + (lc + ld));
+      const float* vs = p.vscale + h * 128;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(o_col + 32 * c, o);
+        tmem_ld_wait();
+        if (query < p.S) {
+          uint4* d4 = reinterpret_cast<uint4*>(p.out + (long long)query * p.ldo + h * 128 + 32 * c);
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          float f[8];
+          for (int q4 = 0; q4 < 4; ++q4) {
+            float f[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(o[q4 * 8 + e]) * inv_l * vs[q4 * 8 + e];
-          d4[q4] = make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]), pack_bf16(f[4], f[5]),
-                              pack_bf16(f[6], f[7]));
+            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(o[q4 * 8 + e]) * inv_l * vs[32 * c + q4 * 8 + e];
+            d4[q4] = make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]), pack_bf16(f[4], f[5]),
+                                pack_bf16(f[6], f[7]));
+          }
         }
       }
     }

@@ -364,6 +364,9 @@ int h3_attn_fp8(const void* q, const void* k, const void* v, long long ld, long 
   if (!q || !k || !v || !out || !workspace) return fail(H3_ERR_ARG, "h3_attn_fp8: NULL pointer");
   if (S <= 0 || H <= 0 || ld % 8 || hstride % 8 || ldo % 8)
     return fail(H3_ERR_SHAPE, "h3_attn_fp8: need strides %% 8 == 0");
+  if (S > AttnSmem::MAX_KBLK * 128 || H > 65535)
+    return fail(H3_ERR_SHAPE, "h3_attn_fp8: S=%d, H=%d beyond the supported S <= %d, H <= 65535", S, H,
+                AttnSmem::MAX_KBLK * 128);
   if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16) || !aligned(workspace, 1024))
     return fail(H3_ERR_ARG, "h3_attn_fp8: q/k/v/out 16-byte and workspace 1024-byte alignment required");
   AttnWs w = attn_ws(S, H);
@@ -396,7 +399,7 @@ int h3_attn_fp8(const void* q, const void* k, const void* v, long long ld, long 
   if ((rc = make_map_u8(&tv, vt8, w.SP, (uint64_t)H * 128, w.SP, 128, 128, "h3_attn_fp8(V)"))) return rc;
   if ((rc = smem_optin(attn_fp8_kernel, AttnSmem::TOTAL, &g_optin_attn, "h3_attn_fp8"))) return rc;
   AttnArgs p{qscale, kscale, vscale, reinterpret_cast<__nv_bfloat16*>(out), ldo, S, w.SP, H};
-  attn_fp8_kernel<<<dim3(w.SP / kQTile, H), kAttnThreads, AttnSmem::TOTAL, st>>>(tq, tk, tv, p);
+  attn_fp8_kernel<<<dim3((S + kQPerCta - 1) / kQPerCta, H), kAttnThreads, AttnSmem::TOTAL, st>>>(tq, tk, tv, p);
   return check_launch("h3_attn_fp8");
 }
 
