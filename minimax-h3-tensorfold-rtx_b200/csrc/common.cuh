@@ -52,20 +52,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// As mbar_try_wait, but a thread whose phase is not complete is suspended until it completes or `ns` nanoseconds
+// pass.  A suspended warp issues nothing: polling warps would otherwise fill the SM sub-partition's memory-I/O queue,
+// which the working warps' TMEM, MUFU and tcgen05.mma instructions also go through.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait until the barrier's phase with the given parity completes.  Gives up after ~2 s of wall time (or at once when
 // another wait of the grid already gave up), records `code` and returns false: every caller then leaves its loop, so
 // a lost arrival ends the kernel with an error status instead of a hang.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr uint32_t kSuspendNs = 1000000u;   // longest single suspension; the limit is checked after each
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
   if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255) == 0) {
-      if (status_bad() || globaltimer() - t0 > kWaitLimitNs) {
-        set_status(code);
-        return false;
-      }
+  const uint64_t t0 = globaltimer();
+  for (;;) {
+    if (mbar_try_wait_suspend(bar, parity, kSuspendNs)) return true;
+    if (status_bad() || globaltimer() - t0 > kWaitLimitNs) {
+      set_status(code);
+      return false;
     }
   }
 }
