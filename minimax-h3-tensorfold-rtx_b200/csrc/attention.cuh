@@ -279,20 +279,23 @@ struct AttnArgs {
 };
 
 constexpr int kAttnStages = 4;
-// One CTA = two 128-row query tiles (A, B) of one head, ping-ponged on the tensor cores: while the softmax of one
-// tile runs, the PV and next QK^T of the other do.  Warps 0-3: softmax of tile A, warps 4-7: tile B -- warp w on TMEM
-// lane quadrant w % 4, one thread per query row holding the row's whole 128-key S tile in registers, so the row max
-// needs no exchange between threads; warp 8: TMA; warp 9: MMA.  TMEM columns: S_A [0, 128), S_B [128, 256),
-// O_A [256, 384), O_B [384, 512); P of keys 32c..32c+31 (e4m3) is written over S columns 32c..32c+7 of its tile.
-constexpr int kAttnThreads = 320;
-constexpr int kProdWarp = 8, kMmaWarp = 9;
+// One CTA = two 128-row query tiles (A, B) of one head.  Each 128-key KV tile is taken in two 64-key halves, and each
+// query tile has two 64-column S buffers in TMEM (one per half), so QK^T of the next half runs on the tensor cores
+// while the softmax of this one does: a group of MMAs takes several hundred cycles from issue to its commit, which
+// then never sits in series with the softmax.  Warps 0-3: softmax of tile A, warps 4-7: tile B -- warp w on TMEM lane
+// quadrant w % 4, one thread per query row, so the row max needs no exchange between threads; warp 8: TMA; warps 9,
+// 10: MMA of tiles A, B (an issuing thread that stops at a barrier lets the tensor pipe run dry; two keep it fed).
+// TMEM columns: S_A [0, 64) and [64, 128), S_B [128, 192) and [192, 256), O_A [256, 384), O_B [384, 512); P of keys
+// 32c..32c+31 of a half (e4m3) is written over columns 32c..32c+7 of its S buffer.
+constexpr int kAttnThreads = 352;
+constexpr int kProdWarp = 8, kMmaWarp = 9;   // MMA warps kMmaWarp + tile
 constexpr int kQTile = 128;
 constexpr int kQPerCta = 2 * kQTile;
 constexpr float kTau = 2.0f;        // running-max lag allowed before O is rescaled (log2 units)
 constexpr float kPOffset = 8.807354922057604f - kTau;   // log2(448) - tau
 // Pairs of each 32-key chunk whose exp2 runs as a polynomial on the FMA pipe instead of the MUFU (bit i: keys 2i,
-// 2i + 1).  The MUFU issues one ex2 per 8 lanes per cycle per SM sub-partition, which bounds an FP8 tile's softmax
-// at about twice the tile's MMA time; moving part of the exponentials to the FMA pipe shortens it.
+// 2i + 1).  The MUFU completes 16 ex2 per cycle per SM, which alone would bound an FP8 tile's softmax at twice the
+// tile's MMA time; moving part of the exponentials to the FMA pipe shortens it.
 constexpr uint32_t kPolyPairs = 0x5252u;
 struct AttnSmem {
   static constexpr int TILE = 128 * 128;
@@ -410,34 +413,39 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* v_full = k_full + kAttnStages;
-  uint64_t* kv_empty = v_full + kAttnStages;
-  uint64_t* s_full = kv_empty + kAttnStages;   // [tile]: QK^T of the tile's current KV tile (and all earlier MMAs) done
-  uint64_t* p_full = s_full + 2;               // [tile]: P written over S by the tile's four softmax warps
-  uint64_t* o_done = p_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
+  uint64_t* kv_full = bars + 1;                // [stage]: K and V^T of a KV tile landed
+  uint64_t* kv_empty = kv_full + kAttnStages;  // [stage]: both tiles' MMAs done reading it
+  uint64_t* s_full = kv_empty + kAttnStages;   // [tile][half]: QK^T of the tile's current KV half landed
+  // [tile][half]: P written over S by the tile's four softmax warps.  One barrier per S buffer: the softmax may
+  // finish half i + 1 before the MMA warp waits for half i, which one barrier's phase parity could not tell apart.
+  uint64_t* p_full = s_full + 4;
+  uint64_t* pv_done = p_full + 4;              // [tile]: one phase per PV of a half
+  uint64_t* o_done = pv_done + 2;              // [tile]: the tile's last PV done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y;
   const int q0 = blockIdx.x * kQPerCta;
   const bool has_b = q0 + kQTile < p.S;       // tile B holds queries of this sequence
   const int nkv = (p.S + 127) / 128;
+  const int nhalf = 2 * nkv;
   float* ksc_s = reinterpret_cast<float*>(smem + L::KSC_OFF);
   for (int i = threadIdx.x; i < nkv; i += blockDim.x) ksc_s[i] = p.kscale[(size_t)h * (p.SP / 128) + i];
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < kAttnStages; ++s) {
-      mbar_init(&k_full[s], 1);
-      mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], has_b ? 2 : 1);   // one commit per MMA warp
     }
     for (int t = 0; t < 2; ++t) {
-      mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 4);   // one arrival per softmax warp of the tile
+      mbar_init(&s_full[2 * t], 1);
+      mbar_init(&s_full[2 * t + 1], 1);
+      mbar_init(&p_full[2 * t], 4);   // one arrival per softmax warp of the tile
+      mbar_init(&p_full[2 * t + 1], 4);
+      mbar_init(&pv_done[t], 1);
+      mbar_init(&o_done[t], 1);
     }
-    mbar_init(o_done, 1);
     fence_barrier_init();
   }
   if (warp == kMmaWarp) {
@@ -450,78 +458,75 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == kProdWarp) {
-    if (lane == 0) {
-      prefetch_tmap(&tmQ);
-      prefetch_tmap(&tmK);
-      prefetch_tmap(&tmV);
+    // TMA producer: the whole warp runs the loop, one lane issues (warp-wide helpers)
+    {
+      if (lane == 0) {
+        prefetch_tmap(&tmQ);
+        prefetch_tmap(&tmK);
+        prefetch_tmap(&tmV);
+      }
       mbar_arrive_expect_tx(q_full, has_b ? 2 * L::TILE : L::TILE);
       tma_load_2d(smem + L::Q_OFF, &tmQ, 0, h * p.SP + q0, q_full);
       if (has_b) tma_load_2d(smem + L::Q_OFF + L::TILE, &tmQ, 0, h * p.SP + q0 + kQTile, q_full);
       for (int j = 0; j < nkv; ++j) {
         const int st = j % kAttnStages;
         const uint32_t ph = (j / kAttnStages) & 1;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1, 201)) break;
+        if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[st], ph ^ 1, 201))) break;
         uint8_t* kv = smem + L::KV_OFF + st * 2 * L::TILE;
-        mbar_arrive_expect_tx(&k_full[st], L::TILE);
-        tma_load_2d(kv, &tmK, 0, h * p.SP + j * 128, &k_full[st]);
-        mbar_arrive_expect_tx(&v_full[st], L::TILE);
-        tma_load_2d(kv + L::TILE, &tmV, j * 128, h * 128, &v_full[st]);
+        mbar_arrive_expect_tx(&kv_full[st], 2 * L::TILE);
+        tma_load_2d(kv, &tmK, 0, h * p.SP + j * 128, &kv_full[st]);
+        tma_load_2d(kv + L::TILE, &tmV, j * 128, h * 128, &kv_full[st]);
       }
     }
-  } else if (warp == kMmaWarp) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_fp8(128, 128);
-      const uint32_t qs = smem_u32(smem + L::Q_OFF);
-      auto issue_s = [&](int t, int st) {   // S_t = Q_t K^T
-        const uint32_t ks = smem_u32(smem + L::KV_OFF + st * 2 * L::TILE);
-        const uint32_t qt = qs + t * L::TILE;
+  } else if (warp == kMmaWarp || warp == kMmaWarp + 1) {
+    const int t = warp - kMmaWarp;   // query tile this warp issues for (the whole warp; one lane issues)
+    if (t == 0 || has_b) {
+      constexpr uint32_t idesc_s = idesc_fp8(128, 64);
+      constexpr uint32_t idesc_o = idesc_fp8(128, 128);
+      const uint32_t qt = smem_u32(smem + L::Q_OFF + t * L::TILE);
+      auto issue_s = [&](int i) {   // S_t[half] = Q_t K[keys of half i]^T (64 K rows = 8 KB into the K tile)
+        const int hf = i & 1;
+        const uint32_t ks = smem_u32(smem + L::KV_OFF + ((i >> 1) % kAttnStages) * 2 * L::TILE) + hf * 64 * 128;
 #pragma unroll
         for (int kb = 0; kb < 4; ++kb)
-          mma_fp8_ss(tmem + t * 128, sdesc_kmajor_sw128(qt + kb * 32), sdesc_kmajor_sw128(ks + kb * 32), idesc, kb != 0);
+          mma_fp8_ss(tmem + t * 128 + hf * 64, sdesc_kmajor_sw128(qt + kb * 32), sdesc_kmajor_sw128(ks + kb * 32),
+                     idesc_s, kb != 0);
       };
-      auto issue_pv = [&](int t, int st, int j) {   // O_t += P_t V
-        const uint32_t vs = smem_u32(smem + L::KV_OFF + st * 2 * L::TILE + L::TILE);
+      auto issue_pv = [&](int i) {   // O_t += P_t[half] V[keys of half i]
+        const int hf = i & 1;
+        const uint32_t vs = smem_u32(smem + L::KV_OFF + ((i >> 1) % kAttnStages) * 2 * L::TILE + L::TILE);
 #pragma unroll
-        for (int kb = 0; kb < 4; ++kb)
-          mma_fp8_ts(tmem + 256 + t * 128, tmem + t * 128 + kb * 32, sdesc_kmajor_sw128(vs + kb * 32), idesc,
-                     (j | kb) != 0);
+        for (int kb = 0; kb < 2; ++kb)
+          mma_fp8_ts(tmem + 256 + t * 128, tmem + t * 128 + hf * 64 + kb * 32,
+                     sdesc_kmajor_sw128(vs + (2 * hf + kb) * 32), idesc_o, (i | kb) != 0);
       };
-      bool ok = mbar_wait(q_full, 0, 202) && mbar_wait(&k_full[0], 0, 203);
+      bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, 202) && mbar_wait(&kv_full[0], 0, 203));
       if (ok) {
         tc_fence_after();
-        issue_s(0, 0);
-        tc_commit(&s_full[0]);
-        if (has_b) {
-          issue_s(1, 0);
-          tc_commit(&s_full[1]);
-        }
+        issue_s(0);
+        tc_commit(&s_full[2 * t]);
+        issue_s(1);
+        tc_commit(&s_full[2 * t + 1]);
       }
-      for (int j = 0; ok && j < nkv; ++j) {
-        const int st = j % kAttnStages;
-        const bool next = j + 1 < nkv;
-        const int st1 = (j + 1) % kAttnStages;
-        if (!(ok = mbar_wait(&p_full[0], j & 1, 204) && mbar_wait(&v_full[st], (j / kAttnStages) & 1, 205))) break;
+      for (int i = 0; ok && i < nhalf; ++i) {
+        const int hf = i & 1, j = i >> 1;
+        const bool more = i + 2 < nhalf;
+        // KV tile j + 1 normally lands long before P_t(i) does: wait for it first, so the MMAs follow P at once
+        if (more && hf == 0 &&
+            !(ok = __all_sync(0xffffffffu,
+                              mbar_wait(&kv_full[(j + 1) % kAttnStages], ((j + 1) / kAttnStages) & 1, 206))))
+          break;
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&p_full[2 * t + hf], (i >> 1) & 1, 204 + t)))) break;
         tc_fence_after();
-        issue_pv(0, st, j);
-        if (!has_b) tc_commit(&kv_empty[st]);
-        if (next) {
-          if (!(ok = mbar_wait(&k_full[st1], ((j + 1) / kAttnStages) & 1, 206))) break;
-          tc_fence_after();
-          issue_s(0, st1);   // after PV_A(j) in issue order, so P_A(j) is consumed before S_A(j + 1) overwrites it
-          tc_commit(&s_full[0]);
-        }
-        if (has_b) {
-          if (!(ok = mbar_wait(&p_full[1], j & 1, 207))) break;
-          tc_fence_after();
-          issue_pv(1, st, j);
-          tc_commit(&kv_empty[st]);
-          if (next) {
-            issue_s(1, st1);
-            tc_commit(&s_full[1]);
-          }
+        issue_pv(i);
+        tc_commit(&pv_done[t]);
+        if (hf == 1) tc_commit(&kv_empty[j % kAttnStages]);
+        if (more) {
+          issue_s(i + 2);   // after PV_t(i) in issue order, so P_t(i) is consumed before S_t(i + 2) overwrites it
+          tc_commit(&s_full[2 * t + hf]);
         }
       }
-      tc_commit(o_done);
+      tc_commit(&o_done[t]);
     }
   } else {
     // ------------------------------------------------------------------ softmax: one thread per query row
@@ -530,35 +535,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int r = qd * 32 + lane;
     const int query = q0 + t * kQTile + r;
     const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
-    const uint32_t s_col = tmem + lane_off + t * 128;
     const uint32_t o_col = tmem + lane_off + 256 + t * 128;
     bool ok = t == 0 || has_b;
     const bool live = ok;
     const float qr = live ? p.qscale[(size_t)h * p.SP + query] : 0.f;
     float m_used = -INFINITY;
     uint64_t l2a = 0, l2b = 0;
-    for (int j = 0; live && j < nkv; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, 210));
+    for (int i = 0; live && i < nhalf; ++i) {
+      const int hf = i & 1;
+      const uint32_t s_col = tmem + lane_off + t * 128 + hf * 64;
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[2 * t + hf], (i >> 1) & 1, 210));
       if (!ok) break;
       tc_fence_after();
-      uint32_t s0[32], s1[32], s2[32], s3[32];
+      uint32_t s0[32], s1[32];
       tmem_ld32(s_col, s0);
       tmem_ld32(s_col + 32, s1);
-      tmem_ld32(s_col + 64, s2);
-      tmem_ld32(s_col + 96, s3);
       tmem_ld_wait();
-      const int valid = p.S - j * 128;   // keys of this KV tile inside the sequence (only the last is ragged)
-      if (valid < 128) {
+      const int valid = p.S - i * 64;   // keys of this half inside the sequence (only the last halves are ragged)
+      if (valid < 64) {
         mask_chunk(s0, valid);
         mask_chunk(s1, valid - 32);
-        mask_chunk(s2, valid - 64);
-        mask_chunk(s3, valid - 96);
       }
-      const float mx = fmaxf(fmaxf(max_chunk(s0, -INFINITY), max_chunk(s1, -INFINITY)),
-                             fmaxf(max_chunk(s2, -INFINITY), max_chunk(s3, -INFINITY)));
-      const float scale = qr * ksc_s[j];
+      const float mx = fmaxf(max_chunk(s0, -INFINITY), max_chunk(s1, -INFINITY));
+      const float scale = qr * ksc_s[i >> 1];
       const float mnew = mx * scale;
-      // raise the running max only when the row's max grew by more than tau (then O and l are rescaled)
+      // raise the running max only when the row's max grew by more than tau (then O and l are rescaled); a half
+      // wholly past the sequence end has mx = -inf and changes nothing
       const bool need = mnew > m_used + kTau;
       float alpha = 1.0f;
       if (need) {
@@ -574,13 +576,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tmem_st8(s_col, pw);
       p_chunk(s1, scale2, nbias2, pw, l2a, l2b);
       tmem_st8(s_col + 32, pw);
-      p_chunk(s2, scale2, nbias2, pw, l2a, l2b);
-      tmem_st8(s_col + 64, pw);
-      p_chunk(s3, scale2, nbias2, pw, l2a, l2b);
-      tmem_st8(s_col + 96, pw);
-      // O holds PV of tiles < j (s_full also tracks PV(j - 1)); the tcgen05 ld/st are warp-wide, so a warp rescales
-      // when any of its rows must (the others multiply by 1)
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
+      // O must hold PV of every half < i before it is rescaled: wait for PV(i - 1) (issued when P(i - 1) was ready,
+      // normally done by now; PV(i - 2) finished before S(i) was computed, so the phase parity is unambiguous).  The
+      // tcgen05 ld/st are warp-wide, so a warp rescales when any of its rows must (the others multiply by 1).
+      if (i > 0 && __any_sync(0xffffffffu, need)) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (i - 1) & 1, 213));
+        if (!ok) break;
+        tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
@@ -594,11 +596,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
+      if (lane == 0) mbar_arrive(&p_full[2 * t + hf]);
     }
     // ---- epilogue: O / l * vscale -> bf16, this thread's row
     if (live) {
-      ok = ok && mbar_wait(o_done, 0, 212);
+      ok = ok && mbar_wait(&o_done[t], 0, 212);
       ok = __all_sync(0xffffffffu, ok);
     }
     if (live && ok) {

@@ -34,8 +34,16 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
+// Issue helpers marked "warp-wide" below are called by all 32 lanes of a converged warp with the same arguments;
+// elect.sync inside the instruction sequence picks the one lane that issues.  The operands then stay in warp-uniform
+// registers: issuing the same instructions from a lane-0 branch instead costs tens of cycles each (a tcgen05.mma
+// from a lane-0 branch takes ~60 cycles to issue, from the whole warp ~7), which starves the tensor pipe.
+#define H3_ELECT "elect.sync rx|e, 0xffffffff;\n\t"
+// warp-wide: one arrival that also expects `bytes` of transaction data
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+  asm volatile("{\n\t.reg .pred e;\n\t.reg .b32 rx;\n\t" H3_ELECT
+               "@e mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n\t}" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -85,21 +93,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int co
 }
 
 // ------------------------------------------------------------------------------------------------ TMA / bulk copies
+// warp-wide: one 2-D tile of a tensor map into shared memory, completing on `bar`
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-      ::"r"(smem_u32(smem_dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      "{\n\t.reg .pred e;\n\t.reg .b32 rx;\n\t" H3_ELECT
+      "@e cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];\n\t}" ::"r"(smem_u32(smem_dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
-__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-      "[%5];" ::"r"(smem_u32(smem_dst)), "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
-      : "memory");
-}
-// Contiguous global -> shared copy; both addresses 16-byte aligned, bytes a multiple of 16.
+// warp-wide: contiguous global -> shared copy; both addresses 16-byte aligned, bytes a multiple of 16
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+  asm volatile("{\n\t.reg .pred e;\n\t.reg .b32 rx;\n\t" H3_ELECT
+               "@e cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n\t}"
                ::"r"(smem_u32(smem_dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
 }
@@ -122,45 +127,50 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// MMA completion -> one arrival on an mbarrier (tracks every tcgen05 op this thread issued before it).
+// warp-wide: MMA completion -> one arrival on an mbarrier (tracks every tcgen05 op the issuing thread issued before
+// it; the elected lane is the same lane each time, as every lane of the warp is active)
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+  asm volatile("{\n\t.reg .pred e;\n\t.reg .b32 rx;\n\t" H3_ELECT
+               "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}"
+               ::"r"(smem_u32(bar))
                : "memory");
 }
 
-// D[tmem] (+)= A[smem] x B[smem]^T with NVFP4 operands and UE4M3 scales per 16 elements read from TMEM.
+// warp-wide: D[tmem] (+)= A[smem] x B[smem]^T with NVFP4 operands and UE4M3 scales per 16 elements read from TMEM
 __device__ __forceinline__ void mma_nvfp4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                           uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 rx;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t" H3_ELECT
+      "@e tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
       ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
       : "memory");
 }
-// D[tmem] (+)= A[smem] x B[smem]^T, e4m3 x e4m3 -> fp32.
+// warp-wide: D[tmem] (+)= A[smem] x B[smem]^T, e4m3 x e4m3 -> fp32
 __device__ __forceinline__ void mma_fp8_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                            uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 rx;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t" H3_ELECT
+      "@e tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-// D[tmem] (+)= A[tmem] x B[smem]^T, e4m3 x e4m3 -> fp32 (A read from TMEM, K-major: lane = row).
+// warp-wide: D[tmem] (+)= A[tmem] x B[smem]^T, e4m3 x e4m3 -> fp32 (A read from TMEM, K-major: lane = row)
 __device__ __forceinline__ void mma_fp8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
                                            uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}"
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 rx;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t" H3_ELECT
+      "@e tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}"
       ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-// 32 lanes x 128 bits from shared memory, replicated to the four 32-lane quadrants of TMEM (scale factors).
+// warp-wide: 32 lanes x 128 bits from shared memory, replicated to the four 32-lane quadrants of TMEM (scale factors)
 __device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+  asm volatile("{\n\t.reg .pred e;\n\t.reg .b32 rx;\n\t" H3_ELECT
+               "@e tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;\n\t}" ::"r"(taddr), "l"(sdesc)
+               : "memory");
 }
 
 // 32 consecutive fp32 columns of this warp's 32 lanes.

@@ -127,10 +127,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      prefetch_tmap(&tmA);
-      prefetch_tmap(&tmB);
+    // ------------------------------------------------------------------ TMA producer (the whole warp; one lane issues)
+    {
+      if (lane == 0) {
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+      }
       uint32_t it = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
@@ -138,7 +140,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int kt = 0; kt < KT; ++kt, ++it) {
           const int s = it % kGemmStages;
           const uint32_t ph = (it / kGemmStages) & 1;
-          if (!(ok = mbar_wait(&empty[s], ph ^ 1, 101))) break;
+          if (!(ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, 101)))) break;
           uint8_t* st = smem + s * L::STAGE_BYTES;
           mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
           tma_load_2d(st, &tmA, kt * 128, m_blk * 128, &full[s]);
@@ -153,18 +155,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------------ MMA issuer (the whole warp; one lane issues)
+    {
       constexpr uint32_t idesc = idesc_nvfp4(128, BN);
       uint32_t it = 0, ti = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x, ++ti) {
-        if (ti > 0 && !(ok = mbar_wait(acc_empty, (ti - 1) & 1, 104))) break;
+        if (ti > 0 && !(ok = __all_sync(0xffffffffu, mbar_wait(acc_empty, (ti - 1) & 1, 104)))) break;
         tc_fence_after();
         for (int kt = 0; kt < KT; ++kt, ++it) {
           const int s = it % kGemmStages;
           const uint32_t ph = (it / kGemmStages) & 1;
-          if (!(ok = mbar_wait(&full[s], ph, 102))) break;
+          if (!(ok = __all_sync(0xffffffffu, mbar_wait(&full[s], ph, 102)))) break;
           tc_fence_after();
           uint8_t* st = smem + s * L::STAGE_BYTES;
           const uint32_t a_s = smem_u32(st), b_s = smem_u32(st + L::A_BYTES);
