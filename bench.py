@@ -282,7 +282,7 @@ def main():
     torch.cuda.set_device(local)
     group = None
     if world > 1:
-        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=600),
+        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300),
                                              device_id=torch.device("cuda", local))
         group = torch.distributed.group.WORLD
     cfg = M.Config(layers=a.layers, dim=5120, heads=40, head_dim=128, ffn=20480, act="gelu", t_dim=8)
