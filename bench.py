@@ -39,6 +39,10 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 METRIC = "s/denoise step, 50-block H3 DiT @37.8k tok, 1/2/4/8 B200; NVFP4 GEMM TFLOPS"
+# DRAM bytes (read + write) of one attention launch per token and head, from the ncu capture summarised in
+# profiles/attn_fp8_s8192_h40.md (181.7 MB at S = 8,192, H = 40).  Traffic grows with S x H, not S^2: the K/V of a
+# head stay in L2 while its CTAs stream them.
+ATTN_DRAM_BYTES_PER_TOKEN_HEAD = 181.7e6 / (8192 * 40)
 SEQ = 37760
 SEGS = (512, 1680, 496, 35072)          # text | keyframe | audio | video (33 latent frames x 24 x 44 patches)
 PEAKS = ROOT / "MEASURED_PEAKS.json"
@@ -208,10 +212,12 @@ def micro(a) -> None:
         ws = torch.empty(N.attn_workspace_bytes(S, H) + 1024, dtype=torch.uint8, device="cuda")
         HD = H * 128
 
+        mask = A.TileMask.block_sparse(S) if a.sparse else None
+
         def run():
-            A.fp8_tokens(qkv[:, :HD], qkv[:, HD:2 * HD], qkv[:, 2 * HD:], S, H, 3 * HD, 128, out, ws)
-        flops = 4.0 * S * S * H * 128
-        what = f"attn S={S} H={H}"
+            A.fp8_tokens(qkv[:, :HD], qkv[:, HD:2 * HD], qkv[:, 2 * HD:], S, H, 3 * HD, 128, out, ws, mask=mask)
+        flops = 4.0 * S * S * H * 128 * (mask.density if mask is not None else 1.0)
+        what = f"attn S={S} H={H}" + (f" block-sparse {mask.density:.3f}" if mask is not None else "")
     else:
         M, Nn, K = (int(v) for v in a.mnk.split(","))
         w = (torch.randn(Nn, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
@@ -266,6 +272,9 @@ def main():
     ap.add_argument("--heads", type=int, default=40)
     ap.add_argument("--mnk", default="37760,15360,5120", help="--micro gemm: M,N,K")
     ap.add_argument("--epi", default="store", choices=["store", "gate", "act_q"])
+    ap.add_argument("--sparse", action="store_true",
+                    help="block-sparse attention (config 4's second run: 25%% of 128x128 tiles per query row, "
+                         "diagonal and text tiles kept, seed 4)")
     a = ap.parse_args()
     if a.impl == "reference":
         return reference_arm(a)
@@ -290,6 +299,9 @@ def main():
     n = S // world
     t0 = n * rank
     eng = M.MiniMaxH3Engine.synthetic(cfg, seed=1, device="cuda", group=group)
+    if a.sparse:
+        from tfvideo import attention as A
+        eng.attn_mask = A.TileMask.block_sparse(S)
     x0 = activations(S, cfg.dim)[t0:t0 + n].cuda()
     t_emb = torch.randn(2, cfg.t_dim, generator=torch.Generator().manual_seed(3)).cuda()
     segs = mod_segments(S)
@@ -375,7 +387,8 @@ def main():
     sustained = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
     per_block = {k: v["ms"] / v["calls"] for k, v in stages.items()}
     Hl = cfg.heads // world
-    attn_flops = 4.0 * S * S * Hl * cfg.head_dim
+    density = eng.attn_mask.density if eng.attn_mask is not None else 1.0
+    attn_flops = 4.0 * S * S * Hl * cfg.head_dim * density   # kept tiles only under the block-sparse mask
     attn_ms = per_block.get("attention", float("nan"))
     gemm_flops = {"gemm_qkv": 2.0 * n * 3 * cfg.inner * cfg.dim, "gemm_out+gate": 2.0 * n * cfg.dim * cfg.inner,
                   "gemm_fc1+act+quant": 2.0 * n * cfg.ffn * cfg.dim, "gemm_fc2+gate": 2.0 * n * cfg.dim * cfg.ffn}
@@ -385,9 +398,12 @@ def main():
     fp8_peak = 2 * sustained
     roofline = {"kernel": "attn_fp8 (tcgen05 FP8 flash attention incl. its prepare)", "bound": "tensor",
                 "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s", "frac": achieved / fp8_peak,
-                "traffic": None,
+                "traffic": ATTN_DRAM_BYTES_PER_TOKEN_HEAD * S * Hl,
+                "traffic_note": "dram read+write per launch: ncu capture at S=8192, H=40 (profiles/"
+                                "attn_fp8_s8192_h40.md) scaled by tokens x heads (K/V of a head stay in L2)",
                 "peak_note": f"2 x {src} bf16 sustained ({sustained} TF/s): dense FP8 = 2 x bf16 on B200",
-                "work_per_launch": f"4*S^2*H*Dh = {attn_flops:.4g} FLOP (S={S}, H={Hl})",
+                "work_per_launch": f"4*S^2*H*Dh*density = {attn_flops:.4g} FLOP (S={S}, H={Hl}, "
+                                   f"tile density {density:.4f})",
                 "nvfp4_gemm": {"achieved": gemm_tflops, "peak": 4 * sustained, "unit": "TFLOP/s",
                                "frac": (gemm_tflops / (4 * sustained)) if gemm_tflops else None,
                                "peak_note": f"4 x {src} bf16 sustained: dense NVFP4 = 4 x bf16 on B200"}}
@@ -406,6 +422,8 @@ def main():
                                        "D=5120, 40x128 heads, GELU-tanh FFN 20480, NVFP4 W4A4 + FP8 attention",
                            "global_batch": 1, "seq_len": S, "layers": cfg.layers,
                            "parallelism": "single GPU" if world == 1 else f"ulysses sp{world} (token-sharded)",
+                           "attention_mask": (f"block-sparse 128x128 tiles, {density:.4f} kept (seed 4)"
+                                              if eng.attn_mask is not None else "dense"),
                            "l2": "inputs larger than L2 (8.9 GB weights + activations per step)"},
                 "stages_ms_per_step": {k: round(v["ms"] / a.steps, 3) for k, v in stages.items()},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,

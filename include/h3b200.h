@@ -134,6 +134,17 @@ size_t h3_attn_workspace_bytes(int S, int H);
 int h3_attn_fp8(const void* q, const void* k, const void* v, long long ld, long long hstride, int S, int H, void* out,
                 long long ldo, void* workspace, size_t workspace_bytes, void* stream);
 
+/* h3_attn_fp8 under a block-sparse mask of 128 x 128 tiles shared by all heads: query tile qt (tokens 128 qt ..
+ * 128 qt + 127) attends only to the KV tiles kv_idx[kv_ptr[qt] .. kv_ptr[qt + 1]) (device int32; kv_ptr has
+ * ceil(S / 128) + 1 entries; each list free of duplicates, any order, entries in [0, ceil(S / 128)); an out-of-range
+ * entry is skipped and recorded in the device status word).  The softmax runs over the kept keys only; a query tile
+ * with an empty list gets zero rows.  This is the "optional block-sparse mask" of the attention path; the reference
+ * takes its sparse attention from ComfyUI's BlockSparseAttention node (tfvideo/minimax_h3.py:285-291 hands the block
+ * to it), which has no in-repository kernel.  Same workspace as h3_attn_fp8. */
+int h3_attn_fp8_sparse(const void* q, const void* k, const void* v, long long ld, long long hstride, int S, int H,
+                       const int* kv_ptr, const int* kv_idx, void* out, long long ldo, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
 /* The same attention as h3_attn_fp8 for callers that cannot allocate device memory -- for example code running
  * inside a host framework that owns every device allocation (ComfyUI records and replays a block's allocations under
  * its dynamic-VRAM mode), or a plugin handed only input and output buffers.  Its scratch is a fixed 64 MiB device

@@ -276,6 +276,10 @@ struct AttnArgs {
   __nv_bfloat16* out;    // element (t, h, d) at out + t * ldo + h * 128 + d
   long long ldo;
   int S, SP, H;
+  // Block-sparse mask (NULL = dense): the KV tiles query tile qt attends to are kv_idx[kv_ptr[qt] .. kv_ptr[qt+1]),
+  // 128-token tiles, shared by all heads.  Sparse launches take one query tile per CTA.
+  const int* kv_ptr;
+  const int* kv_idx;
 };
 
 constexpr int kAttnStages = 4;
@@ -303,7 +307,8 @@ struct AttnSmem {
   static constexpr int KV_OFF = 2 * TILE;                               // per stage: K, V^T
   static constexpr int KSC_OFF = KV_OFF + kAttnStages * 2 * TILE;       // this head's K-block scales
   static constexpr int MAX_KBLK = 2048;                                 // sequences up to 262,144 tokens
-  static constexpr int BAR_OFF = KSC_OFF + MAX_KBLK * 4;
+  static constexpr int KVT_OFF = KSC_OFF + MAX_KBLK * 4;                // KV tile of each step (block-sparse)
+  static constexpr int BAR_OFF = KVT_OFF + MAX_KBLK * 4;
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;
 };
 
@@ -425,12 +430,33 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y;
-  const int q0 = blockIdx.x * kQPerCta;
-  const bool has_b = q0 + kQTile < p.S;       // tile B holds queries of this sequence
-  const int nkv = (p.S + 127) / 128;
+  const bool sparse = p.kv_ptr != nullptr;
+  const int q0 = blockIdx.x * (sparse ? kQTile : kQPerCta);
+  const bool has_b = !sparse && q0 + kQTile < p.S;   // tile B holds queries of this sequence
+  const int nkt = (p.S + 127) / 128;                  // KV tiles of the sequence
+  // the CTA's KV steps: every KV tile in order (dense), or the query tile's list (block-sparse); step j reads KV tile
+  // kvt_s[j] with K-block scale ksc_s[j].  An out-of-range list entry is recorded in the status word and skipped.
+  int nkv = nkt;
+  int kv0 = 0;
+  if (sparse) {
+    kv0 = p.kv_ptr[blockIdx.x];
+    nkv = min(max(p.kv_ptr[blockIdx.x + 1] - kv0, 0), L::MAX_KBLK);
+  }
   const int nhalf = 2 * nkv;
   float* ksc_s = reinterpret_cast<float*>(smem + L::KSC_OFF);
-  for (int i = threadIdx.x; i < nkv; i += blockDim.x) ksc_s[i] = p.kscale[(size_t)h * (p.SP / 128) + i];
+  int* kvt_s = reinterpret_cast<int*>(smem + L::KVT_OFF);
+  for (int i = threadIdx.x; i < nkv; i += blockDim.x) {
+    int kt = i;
+    if (sparse) {
+      kt = p.kv_idx[kv0 + i];
+      if (kt < 0 || kt >= nkt) {
+        set_status(220);
+        kt = -1;
+      }
+    }
+    kvt_s[i] = kt;
+    ksc_s[i] = kt >= 0 ? p.kscale[(size_t)h * (p.SP / 128) + kt] : 0.f;
+  }
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -465,17 +491,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         prefetch_tmap(&tmK);
         prefetch_tmap(&tmV);
       }
-      mbar_arrive_expect_tx(q_full, has_b ? 2 * L::TILE : L::TILE);
-      tma_load_2d(smem + L::Q_OFF, &tmQ, 0, h * p.SP + q0, q_full);
-      if (has_b) tma_load_2d(smem + L::Q_OFF + L::TILE, &tmQ, 0, h * p.SP + q0 + kQTile, q_full);
+      if (nkv > 0) {   // (nothing waits for Q when there is no KV step, so nothing is loaded)
+        mbar_arrive_expect_tx(q_full, has_b ? 2 * L::TILE : L::TILE);
+        tma_load_2d(smem + L::Q_OFF, &tmQ, 0, h * p.SP + q0, q_full);
+        if (has_b) tma_load_2d(smem + L::Q_OFF + L::TILE, &tmQ, 0, h * p.SP + q0 + kQTile, q_full);
+      }
       for (int j = 0; j < nkv; ++j) {
         const int st = j % kAttnStages;
         const uint32_t ph = (j / kAttnStages) & 1;
         if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[st], ph ^ 1, 201))) break;
         uint8_t* kv = smem + L::KV_OFF + st * 2 * L::TILE;
         mbar_arrive_expect_tx(&kv_full[st], 2 * L::TILE);
-        tma_load_2d(kv, &tmK, 0, h * p.SP + j * 128, &kv_full[st]);
-        tma_load_2d(kv + L::TILE, &tmV, j * 128, h * 128, &kv_full[st]);
+        const int kt = max(kvt_s[j], 0);
+        tma_load_2d(kv, &tmK, 0, h * p.SP + kt * 128, &kv_full[st]);
+        tma_load_2d(kv + L::TILE, &tmV, kt * 128, h * 128, &kv_full[st]);
       }
     }
   } else if (warp == kMmaWarp || warp == kMmaWarp + 1) {
@@ -500,7 +529,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           mma_fp8_ts(tmem + 256 + t * 128, tmem + t * 128 + hf * 64 + kb * 32,
                      sdesc_kmajor_sw128(vs + (2 * hf + kb) * 32), idesc_o, (i | kb) != 0);
       };
-      bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, 202) && mbar_wait(&kv_full[0], 0, 203));
+      // (a query tile with no KV tile -- an empty block-sparse row -- issues nothing; its output rows are zero)
+      bool ok = nhalf > 0 && __all_sync(0xffffffffu, mbar_wait(q_full, 0, 202) && mbar_wait(&kv_full[0], 0, 203));
       if (ok) {
         tc_fence_after();
         issue_s(0);
@@ -551,7 +581,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tmem_ld32(s_col, s0);
       tmem_ld32(s_col + 32, s1);
       tmem_ld_wait();
-      const int valid = p.S - i * 64;   // keys of this half inside the sequence (only the last halves are ragged)
+      // keys of this half inside the sequence (only the last KV tile is ragged; a skipped list entry has none)
+      const int kt = kvt_s[i >> 1];
+      const int valid = kt < 0 ? 0 : p.S - kt * 128 - hf * 64;
       if (valid < 64) {
         mask_chunk(s0, valid);
         mask_chunk(s1, valid - 32);
@@ -608,7 +640,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       float la, lb, lc, ld;
       f32x2_unpack(l2a, la, lb);
       f32x2_unpack(l2b, lc, ld);
-      const float inv_l = 1.0f / ((la + lb) + (lc + ld));
+      const float inv_l = nhalf > 0 ? 1.0f / ((la + lb) + (lc + ld)) : 0.0f;
       const float* vs = p.vscale + h * 128;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
@@ -621,7 +653,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int q4 = 0; q4 < 4; ++q4) {
             float f[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(o[q4 * 8 + e]) * inv_l * vs[32 * c + q4 * 8 + e];
+            for (int e = 0; e < 8; ++e)
+              f[e] = nhalf > 0 ? __uint_as_float(o[q4 * 8 + e]) * inv_l * vs[32 * c + q4 * 8 + e] : 0.0f;
             d4[q4] = make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]), pack_bf16(f[4], f[5]),
                                 pack_bf16(f[6], f[7]));
           }

@@ -359,19 +359,22 @@ size_t h3_attn_workspace_bytes(int S, int H) {
   return attn_ws(S, H).total;
 }
 
-int h3_attn_fp8(const void* q, const void* k, const void* v, long long ld, long long hstride, int S, int H, void* out,
-                long long ldo, void* workspace, size_t workspace_bytes, void* stream) {
-  if (!q || !k || !v || !out || !workspace) return fail(H3_ERR_ARG, "h3_attn_fp8: NULL pointer");
+namespace {
+// Prepare (K mean / V max, FP8 quantisation) and the attention kernel, dense (kv_ptr NULL) or block-sparse.
+int attn_run(const char* who, const void* q, const void* k, const void* v, long long ld, long long hstride, int S,
+             int H, const int* kv_ptr, const int* kv_idx, void* out, long long ldo, void* workspace,
+             size_t workspace_bytes, void* stream) {
+  if (!q || !k || !v || !out || !workspace) return fail(H3_ERR_ARG, "%s: NULL pointer", who);
   if (S <= 0 || H <= 0 || ld % 8 || hstride % 8 || ldo % 8)
-    return fail(H3_ERR_SHAPE, "h3_attn_fp8: need strides %% 8 == 0");
+    return fail(H3_ERR_SHAPE, "%s: need strides %% 8 == 0", who);
   if (S > AttnSmem::MAX_KBLK * 128 || H > 65535)
-    return fail(H3_ERR_SHAPE, "h3_attn_fp8: S=%d, H=%d beyond the supported S <= %d, H <= 65535", S, H,
+    return fail(H3_ERR_SHAPE, "%s: S=%d, H=%d beyond the supported S <= %d, H <= 65535", who, S, H,
                 AttnSmem::MAX_KBLK * 128);
   if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16) || !aligned(workspace, 1024))
-    return fail(H3_ERR_ARG, "h3_attn_fp8: q/k/v/out 16-byte and workspace 1024-byte alignment required");
+    return fail(H3_ERR_ARG, "%s: q/k/v/out 16-byte and workspace 1024-byte alignment required", who);
   AttnWs w = attn_ws(S, H);
   if (workspace_bytes < w.total)
-    return fail(H3_ERR_ARG, "h3_attn_fp8: workspace %zu bytes < %zu", workspace_bytes, w.total);
+    return fail(H3_ERR_ARG, "%s: workspace %zu bytes < %zu", who, workspace_bytes, w.total);
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
   uint8_t* q8 = ws + w.q8;
   uint8_t* k8 = ws + w.k8;
@@ -387,20 +390,38 @@ int h3_attn_fp8(const void* q, const void* k, const void* v, long long ld, long 
                 reinterpret_cast<const __nv_bfloat16*>(v), ld, hstride};
   cudaStream_t st = S_(stream);
   attn_stats_kernel<<<dim3(w.nblk, H), 128, 0, st>>>(view, S, H, ksum, vmax);
-  int rc = check_launch("h3_attn_fp8(stats)");
+  int rc = check_launch(who);
   if (rc) return rc;
   attn_stats_reduce_kernel<<<(H * 128 + 127) / 128, 128, 0, st>>>(ksum, vmax, w.nblk, S, H, kmean, vscale, vinv);
-  if ((rc = check_launch("h3_attn_fp8(reduce)"))) return rc;
+  if ((rc = check_launch(who))) return rc;
   attn_quant_kernel<<<dim3(w.SP / 128, H), 128, 0, st>>>(view, S, w.SP, H, kmean, vinv, q8, qscale, k8, kscale, vt8);
-  if ((rc = check_launch("h3_attn_fp8(quant)"))) return rc;
+  if ((rc = check_launch(who))) return rc;
   CUtensorMap tq, tk, tv;
-  if ((rc = make_map_u8(&tq, q8, 128, (uint64_t)H * w.SP, 128, 128, 128, "h3_attn_fp8(Q)"))) return rc;
-  if ((rc = make_map_u8(&tk, k8, 128, (uint64_t)H * w.SP, 128, 128, 128, "h3_attn_fp8(K)"))) return rc;
-  if ((rc = make_map_u8(&tv, vt8, w.SP, (uint64_t)H * 128, w.SP, 128, 128, "h3_attn_fp8(V)"))) return rc;
-  if ((rc = smem_optin(attn_fp8_kernel, AttnSmem::TOTAL, &g_optin_attn, "h3_attn_fp8"))) return rc;
-  AttnArgs p{qscale, kscale, vscale, reinterpret_cast<__nv_bfloat16*>(out), ldo, S, w.SP, H};
-  attn_fp8_kernel<<<dim3((S + kQPerCta - 1) / kQPerCta, H), kAttnThreads, AttnSmem::TOTAL, st>>>(tq, tk, tv, p);
-  return check_launch("h3_attn_fp8");
+  if ((rc = make_map_u8(&tq, q8, 128, (uint64_t)H * w.SP, 128, 128, 128, who))) return rc;
+  if ((rc = make_map_u8(&tk, k8, 128, (uint64_t)H * w.SP, 128, 128, 128, who))) return rc;
+  if ((rc = make_map_u8(&tv, vt8, w.SP, (uint64_t)H * 128, w.SP, 128, 128, who))) return rc;
+  if ((rc = smem_optin(attn_fp8_kernel, AttnSmem::TOTAL, &g_optin_attn, who))) return rc;
+  AttnArgs p{qscale, kscale, vscale, reinterpret_cast<__nv_bfloat16*>(out), ldo, S, w.SP, H, kv_ptr, kv_idx};
+  const int qtiles_per_cta = kv_ptr ? kQTile : kQPerCta;   // block-sparse launches take one query tile per CTA
+  attn_fp8_kernel<<<dim3((S + qtiles_per_cta - 1) / qtiles_per_cta, H), kAttnThreads, AttnSmem::TOTAL, st>>>(tq, tk,
+                                                                                                         tv, p);
+  return check_launch(who);
+}
+}  // namespace
+
+int h3_attn_fp8(const void* q, const void* k, const void* v, long long ld, long long hstride, int S, int H, void* out,
+                long long ldo, void* workspace, size_t workspace_bytes, void* stream) {
+  return attn_run("h3_attn_fp8", q, k, v, ld, hstride, S, H, nullptr, nullptr, out, ldo, workspace, workspace_bytes,
+                  stream);
+}
+
+int h3_attn_fp8_sparse(const void* q, const void* k, const void* v, long long ld, long long hstride, int S, int H,
+                       const int* kv_ptr, const int* kv_idx, void* out, long long ldo, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  if (!kv_ptr || !kv_idx) return fail(H3_ERR_ARG, "h3_attn_fp8_sparse: NULL tile list");
+  if (!aligned(kv_ptr, 4) || !aligned(kv_idx, 4)) return fail(H3_ERR_ARG, "h3_attn_fp8_sparse: misaligned tile list");
+  return attn_run("h3_attn_fp8_sparse", q, k, v, ld, hstride, S, H, kv_ptr, kv_idx, out, ldo, workspace,
+                  workspace_bytes, stream);
 }
 
 }  // extern "C"

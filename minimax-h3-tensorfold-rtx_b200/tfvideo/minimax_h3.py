@@ -124,7 +124,8 @@ class _Buffers:
 
 
 class MiniMaxH3Engine:
-    """The DiT blocks with NVFP4 linears on B200; ``attn`` picks the attention backend (fp8 by default)."""
+    """The DiT blocks with NVFP4 linears on B200; ``attn`` picks the attention backend (fp8 by default).
+    ``attn_mask`` (an attention.TileMask for the sequence length) runs the FP8 attention block-sparse."""
 
     MLP_CHUNK = None                      # the whole sequence at once (HBM holds it)
 
@@ -150,6 +151,7 @@ class MiniMaxH3Engine:
         self._rope_key = self._rope = None
         self.clipped = torch.zeros((), dtype=torch.int32, device=self.device)
         self.timer = None                  # a profiling.StageTimer to time each stage of each block
+        self.attn_mask = None              # attention.TileMask: block-sparse FP8 attention when set
 
     # ------------------------------------------------------------------ construction
     @classmethod
@@ -324,7 +326,12 @@ class MiniMaxH3Engine:
         return self._mlp_half(i, b, x, mod, idx, buf, delayed)
 
     def _attend(self, q, k, v, S, H, ld, out, ws):
-        if self.attn is A.fp8:
+        m = self.attn_mask
+        if self.attn is A.fp8 and m is not None:
+            if m.S != S:
+                raise ValueError(f"attn_mask is for S={m.S}, the sequence has S={S}")
+            N.attn_fp8_sparse(q, k, v, ld, self.cfg.head_dim, S, H, m.kv_ptr, m.kv_idx, out, out.stride(0), ws)
+        elif self.attn is A.fp8:
             N.attn_fp8(q, k, v, ld, self.cfg.head_dim, S, H, out, out.stride(0), ws)
         else:   # a library backend (sdpa / cudnn), for comparisons
             Dh = self.cfg.head_dim

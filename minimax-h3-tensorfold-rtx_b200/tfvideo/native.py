@@ -47,6 +47,7 @@ _SIGS = {
     "h3_attn_workspace_bytes": ([i32, i32], sz),
     "h3_attn_fp8": [vp, vp, vp, i64, i64, i32, i32, vp, i64, vp, sz, vp],
     "h3_attn_fp8_noalloc": [vp, vp, vp, i64, i64, i32, i32, vp, i64, vp],
+    "h3_attn_fp8_sparse": [vp, vp, vp, i64, i64, i32, i32, vp, vp, vp, i64, vp, sz, vp],
 }
 
 _lib = None
@@ -197,3 +198,10 @@ def attn_fp8(q, k, v, ld, hstride, S, H, out, ldo, workspace) -> None:
     _count(4)
     check(lib().h3_attn_fp8(ptr(q), ptr(k), ptr(v), ld, hstride, S, H, ptr(out), ldo, ptr(workspace),
                             workspace.numel() * workspace.element_size(), stream()), "h3_attn_fp8")
+
+
+def attn_fp8_sparse(q, k, v, ld, hstride, S, H, kv_ptr, kv_idx, out, ldo, workspace) -> None:
+    _count(4)
+    check(lib().h3_attn_fp8_sparse(ptr(q), ptr(k), ptr(v), ld, hstride, S, H, ptr(kv_ptr), ptr(kv_idx), ptr(out), ldo,
+                                   ptr(workspace), workspace.numel() * workspace.element_size(), stream()),
+          "h3_attn_fp8_sparse")

@@ -192,18 +192,37 @@ def linear_bf16(x, w, bias=None) -> np.ndarray:
 
 
 # ------------------------------------------------------------------------------------------ attention
-def sdpa(q, k, v) -> np.ndarray:
-    """softmax(q k^T / sqrt(Dh)) v in fp32 (torch CPU), [H, S, Dh] (tfvideo/attention.py:17-26)."""
+def tile_key_mask(lists, S: int, tile: int = 128) -> torch.Tensor:
+    """Boolean [S, S] key mask of a block-sparse tile mask: query tile r keeps the KV tiles in lists[r].  The block-
+    sparse mask of BASELINE's sharded config (128 x 128 tiles, shared by all heads); the reference takes its sparse
+    attention from ComfyUI's BlockSparseAttention node (called through tfvideo/minimax_h3.py:285-291)."""
+
+    keep = torch.zeros(S, S, dtype=torch.bool)
+    for r, row in enumerate(lists):
+        for c in row:
+            keep[r * tile:(r + 1) * tile, c * tile:(c + 1) * tile] = True
+    return keep
+
+
+def sdpa(q, k, v, tile_lists=None) -> np.ndarray:
+    """softmax(q k^T / sqrt(Dh)) v in fp32 (torch CPU), [H, S, Dh] (tfvideo/attention.py:17-26); under a block-sparse
+    tile mask when ``tile_lists`` is given (rows with no kept key give zeros)."""
 
     q, k, v = (torch.from_numpy(f32(t)) for t in (q, k, v))
-    return torch.nn.functional.scaled_dot_product_attention(q, k, v).numpy()
+    if tile_lists is None:
+        return torch.nn.functional.scaled_dot_product_attention(q, k, v).numpy()
+    keep = tile_key_mask(tile_lists, q.shape[1])
+    s = (q @ k.transpose(1, 2)) / math.sqrt(q.shape[2])
+    s = s.masked_fill(~keep, float("-inf"))
+    p = torch.softmax(s, -1).nan_to_num(0.0)
+    return (p @ v).numpy()
 
 
 def _e4m3(t: torch.Tensor) -> torch.Tensor:
     return t.clamp(-448.0, 448.0).to(torch.float8_e4m3fn).float()
 
 
-def attention_fp8(q, k, v, blk: int = 128) -> np.ndarray:
+def attention_fp8(q, k, v, blk: int = 128, tile_lists=None) -> np.ndarray:
     """The FP8 attention recipe of the CUDA kernel, with exact (not online) softmax, [H, S, Dh] -> bf16 values.
 
     Follows tfvideo/fp4attn.py:82-147,170-238 (qk="fp8", pv="fp8"): K smoothed by its per-channel mean over the
@@ -227,11 +246,13 @@ def attention_fp8(q, k, v, blk: int = 128) -> np.ndarray:
     k8 = _e4m3(ks * (1.0 / krow))
     v8 = _e4m3(v * (448.0 / vmax))
     s = (q8 @ k8.transpose(1, 2)) * qr * krow.transpose(1, 2)
+    if tile_lists is not None:   # block-sparse: the softmax runs over the kept keys only
+        s = s.masked_fill(~tile_key_mask(tile_lists, S, blk), float("-inf"))
     m = s.amax(-1, keepdim=True)
-    p = torch.exp2(s - m)
+    p = torch.exp2(s - m).nan_to_num(0.0)
     l = p.sum(-1, keepdim=True)
     p8 = _e4m3(p * 448.0)
-    o = (p8 @ v8) * (vmax / (448.0 * 448.0)) / l
+    o = (p8 @ v8) * (vmax / (448.0 * 448.0)) / l.clamp_min(1e-30)
     return bf16_round(o.numpy())
 
 

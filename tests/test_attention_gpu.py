@@ -114,3 +114,65 @@ def test_attention_deterministic():
     a, b = A.fp8(q, k, v), A.fp8(q, k, v)
     assert torch.equal(a, b)
     _ = math
+
+
+# ------------------------------------------------------------------------------------------------ block-sparse
+def _random_lists(nt: int, seed: int, keep: float, empty_row: int | None = None):
+    rs = np.random.RandomState(seed)
+    lists = []
+    for r in range(nt):
+        if r == empty_row:
+            lists.append([])
+            continue
+        row = {r} | set(rs.choice(nt, size=max(1, int(keep * nt)), replace=False).tolist())
+        lists.append(sorted(row, reverse=bool(r % 2)))   # any order is allowed
+    return lists
+
+
+@pytest.mark.parametrize("S,H,keep", [(1000, 3, 0.4), (4096, 4, 0.25)])
+def test_attention_block_sparse_vs_masked_references(S, H, keep):
+    """Block-sparse FP8 attention against fp32 SDPA and the FP8 recipe under the same 128 x 128 tile mask."""
+
+    from tfvideo import attention as A
+
+    nt = (S + 127) // 128
+    lists = _random_lists(nt, 5, keep, empty_row=1)
+    m = A.TileMask(lists, S)
+    q, k, v = _normed(H, S, 1), _normed(H, S, 2, bias=1.0), _normed(H, S, 3)
+    got = to_np(A.fp8(*(to_dev(t)[None] for t in (q, k, v)), mask=m)[0])
+    device_ok()
+    assert np.isfinite(got).all()
+    assert not got[:, 128:256].any()                      # the empty query tile gives zero rows
+    live = np.ones(S, dtype=bool)
+    live[128:256] = False
+    ref = OO.sdpa(q, k, v, tile_lists=lists)
+    c = OO.cosine(got[:, live], ref[:, live])
+    assert c >= 0.998, f"cos {c:.6f}"
+    assert OO.cosine(got[:, live], OO.attention_fp8(q, k, v, tile_lists=lists)[:, live]) >= 0.998
+
+
+def test_attention_block_sparse_full_mask_equals_dense():
+    """Every tile kept: the one-query-tile-per-CTA sparse launch computes each row exactly as the dense launch."""
+
+    from tfvideo import attention as A
+
+    S, H = 777, 2
+    nt = (S + 127) // 128
+    m = A.TileMask([list(range(nt))] * nt, S)
+    q, k, v = (to_dev(_normed(H, S, s))[None] for s in (7, 8, 9))
+    assert torch.equal(A.fp8(q, k, v, mask=m), A.fp8(q, k, v))
+    device_ok()
+
+
+def test_attention_block_sparse_config_mask():
+    """BASELINE's sharded-config mask: 25% of tiles per query row, diagonal and text tiles kept."""
+
+    from tfvideo import attention as A
+
+    S, H = 2048, 2
+    m = A.TileMask.block_sparse(S, keep=0.25, text_tokens=512, seed=4)
+    assert all(r in row and {0, 1, 2, 3} <= set(row) for r, row in enumerate(m.lists))
+    q, k, v = _normed(H, S, 11), _normed(H, S, 12), _normed(H, S, 13)
+    got = to_np(A.fp8(*(to_dev(t)[None] for t in (q, k, v)), mask=m)[0])
+    device_ok()
+    assert OO.cosine(got, OO.sdpa(q, k, v, tile_lists=m.lists)) >= 0.998
