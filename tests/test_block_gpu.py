@@ -102,3 +102,29 @@ def test_engine_bf16_residual_contract():
     with pytest.raises(ValueError):
         M.EngineBlock(eng, 0)(xt.float(), to_dev(t_emb, torch.float32), segs,
                               to_dev(rope, torch.float32).reshape(1, 128, 1, 64, 2, 2))
+
+
+def test_step_graph_replays_match_eager_forwards():
+    """A captured delayed-scale step replays bit for bit what eager forwards compute from the same state."""
+
+    from tfvideo import graph as G
+
+    M, cfg, eng, shape, p, x, t_emb, segs, rope = _setup("gelu", 384, 128)
+    rope_t = to_dev(rope, torch.float32).reshape(1, 384, 1, 64, 2, 2)
+    te = to_dev(t_emb, torch.float32)
+    xs = [to_dev(bf16_array((384, cfg.dim), s)) for s in (21, 22, 23)]
+
+    eager = []
+    for xi in xs:                                   # forward 1 (dynamic scales), then 2 and 3 (delayed)
+        eager.append(to_np(eng.forward(xi.clone(), te, segs, rope_t)))
+    eng.end_run()
+    eng.forward(xs[0].clone(), te, segs, rope_t)    # forward 1 of a new run, eager
+    g = G.StepGraph(eng, xs[1], te, segs, rope_t)
+    got = []
+    for xi in xs[1:]:
+        g.x.copy_(xi)
+        got.append(to_np(g.replay()))
+    torch.cuda.synchronize()
+    device_ok()
+    assert np.array_equal(got[0], eager[1])
+    assert np.array_equal(got[1], eager[2])
