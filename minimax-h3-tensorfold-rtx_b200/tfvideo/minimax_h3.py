@@ -108,9 +108,7 @@ class _Buffers:
         self.a4sf = torch.zeros(N.sf_tiled_bytes(n, F), dtype=torch.uint8, **e)
         self.mod = torch.empty((M, 18 * D), dtype=torch.float32, **e)
         if world > 1:
-            self.q_all = torch.empty((S, Hl, cfg.head_dim), dtype=torch.bfloat16, **e)
-            self.k_all = torch.empty_like(self.q_all)
-            self.v_all = torch.empty_like(self.q_all)
+            self.qkv_all = torch.empty((S, 3, Hl, cfg.head_dim), dtype=torch.bfloat16, **e)
             self.o_recv = torch.empty((world, n, Hl * cfg.head_dim), dtype=torch.bfloat16, **e)
         self._dyn = None
 
@@ -303,11 +301,11 @@ class MiniMaxH3Engine:
         else:
             Hl = H // world
             with maybe(T, "all_to_all"):
-                self.sp.heads_from_tokens(q.view(n, H, Dh), buf.q_all)
-                self.sp.heads_from_tokens(k.view(n, H, Dh), buf.k_all)
-                self.sp.heads_from_tokens(v.view(n, H, Dh), buf.v_all)
+                self.sp.qkv_heads_from_tokens(buf.qkv.view(n, 3, H, Dh), buf.qkv_all)
+            qa = buf.qkv_all.view(S, 3 * Hl * Dh)
             with maybe(T, "attention"):
-                self._attend(buf.q_all, buf.k_all, buf.v_all, S, Hl, Hl * Dh, buf.o, ws)
+                self._attend(qa[:, :Hl * Dh], qa[:, Hl * Dh:2 * Hl * Dh], qa[:, 2 * Hl * Dh:], S, Hl, 3 * Hl * Dh,
+                             buf.o, ws)
             with maybe(T, "all_to_all"):
                 self.sp.tokens_from_heads(buf.o, buf.o_recv)
             src = dict(x=buf.o_recv, R=n, K=HD, ldx=Hl * Dh, cblk=Hl * Dh, blk_stride=n * Hl * Dh)

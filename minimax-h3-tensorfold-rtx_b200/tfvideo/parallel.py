@@ -38,6 +38,19 @@ class SequenceParallel:
         dist.all_to_all_single(out.view(P, n, H // P, Dh), send, group=self.group)
         return out
 
+    def qkv_heads_from_tokens(self, qkv: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """qkv [S/P, 3, H, Dh] (the qkv GEMM's rows) -> out [S, 3, H/P, Dh]: q, k and v of this rank's heads for every
+        token, in one all-to-all.  The result has the qkv buffer's own row layout, so attention reads q / k / v from
+        it with row stride 3 (H/P) Dh, as it reads the single-GPU qkv buffer."""
+
+        P = self.world
+        n, three, H, Dh = qkv.shape
+        if H % P:
+            raise ValueError(f"{H} heads do not split over {P} ranks")
+        send = qkv.reshape(n, 3, P, H // P, Dh).permute(2, 0, 1, 3, 4).contiguous()
+        dist.all_to_all_single(out.view(P, n, 3, H // P, Dh), send, group=self.group)
+        return out
+
     def tokens_from_heads(self, o: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         """o [S, H/P * Dh] -> out [P, S/P, H/P * Dh]: this rank's tokens, column block r from rank r's heads."""
 

@@ -1,0 +1,41 @@
+"""Worker of tests/test_parallel_gpu.py (run under torchrun): the Ulysses engine on WORLD_SIZE GPUs against the
+single-GPU engine on the same seeded inputs and weights, over three forwards (dynamic, then delayed scales)."""
+import os, sys
+from datetime import timedelta
+root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, os.path.join(root, "minimax-h3-tensorfold-rtx_b200")); sys.path.insert(0, root)
+import torch, torch.distributed as dist
+rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+torch.cuda.set_device(local)
+dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+from tfvideo import minimax_h3 as M, native as N
+cfg = M.Config(layers=2, dim=512, heads=8, head_dim=128, ffn=1024, act="gelu", t_dim=8)
+S = 1024
+g = torch.Generator().manual_seed(5)
+x = torch.randn(S, cfg.dim, generator=g).to(torch.bfloat16).cuda()
+t_emb = torch.randn(2, cfg.t_dim, generator=g).cuda()
+segs = [(0, 100, 0), (100, S, 3)]
+rot = 128
+ang = torch.randn(S, rot // 2, generator=g)
+rope = torch.stack([torch.stack([ang.cos(), -ang.sin()], -1), torch.stack([ang.sin(), ang.cos()], -1)], -2)
+rope = rope.reshape(1, S, 1, rot // 2, 2, 2).cuda()
+eng = M.MiniMaxH3Engine.synthetic(cfg, seed=1, device="cuda", group=dist.group.WORLD)
+n = S // world
+outs = []
+for f in range(3):
+    xs = x[rank * n:(rank + 1) * n].clone()
+    outs.append(eng.forward(xs, t_emb, segs, rope).clone())
+gath = [torch.empty_like(outs[-1]) for _ in range(world)]
+dist.all_gather(gath, outs[-1])
+full_sp = torch.cat(gath)
+if rank == 0:
+    ref = M.MiniMaxH3Engine.from_weights(M.synthetic_weights(cfg, 1, "cuda"), cfg, device="cuda")
+    ref.sp = None
+    for f in range(3):
+        r = ref.forward(x.clone(), t_emb, segs, rope)
+    torch.cuda.synchronize()
+    eq = torch.equal(full_sp, r)
+    cos = torch.nn.functional.cosine_similarity(full_sp.float().flatten(), r.float().flatten(), dim=0).item()
+    print(f"RESULT world={world} bitwise={eq} cosine={cos:.8f} status={N.device_status()}", flush=True)
+dist.barrier()
+dist.destroy_process_group()

@@ -53,6 +53,11 @@ def _ulysses_worker(rank, world, port, q):
             ref = qkv[:, j, rank * (H // world):(rank + 1) * (H // world)]
             assert torch.equal(buf, ref), f"rank {rank}: head gather mismatch for tensor {j}"
             outs.append(buf)
+        # the engine's form: q, k and v in one all-to-all, received in the qkv buffer's row layout
+        both = torch.empty(S, 3, H // world, Dh)
+        sp.qkv_heads_from_tokens(local.contiguous(), both)
+        for j in range(3):
+            assert torch.equal(both[:, j], outs[j]), f"rank {rank}: fused q/k/v exchange differs for tensor {j}"
         # attention on this rank's heads over the full sequence, then back to token-sharded rows
         qh, kh, vh = (t.transpose(0, 1) for t in outs)
         o = torch.nn.functional.scaled_dot_product_attention(qh, kh, vh).transpose(0, 1).reshape(S, -1)
