@@ -128,6 +128,27 @@ class Nvfp4Linear(Linear):
         if act is not None:
             self.set_act(act)
 
+    @classmethod
+    def from_quantized(cls, codes: torch.Tensor, sf: torch.Tensor, g: float, n: int, k: int,
+                       interleaved: bool = False, slots: torch.Tensor | None = None, slot: int = 0,
+                       bias: torch.Tensor | None = None) -> "Nvfp4Linear":
+        """A linear from already quantised weights (codes [N, K/2] u8, tiled scales, global scale g): how a converted
+        engine is loaded back."""
+
+        if not nvfp4_supported():
+            raise RuntimeError("Nvfp4Linear needs a B200 (compute capability 10.x)")
+        lin = cls.__new__(cls)
+        lin.n, lin.k, lin.g, lin.interleaved = int(n), int(k), float(g), bool(interleaved)
+        lin.codes = codes.to(device="cuda", dtype=torch.uint8).contiguous()
+        lin.sf = sf.to(device="cuda", dtype=torch.uint8).contiguous()
+        if tuple(lin.codes.shape) != (lin.n, lin.k // 2) or lin.sf.numel() != N.sf_tiled_bytes(lin.n, lin.k):
+            raise ValueError(f"Nvfp4Linear.from_quantized: tensors do not match [{n}, {k}]")
+        lin.bias = None if bias is None else bias.to(device="cuda", dtype=torch.float32).contiguous()
+        lin.slots = new_slots(1, lin.codes.device) if slots is None else slots
+        lin.slot = slot
+        lin.dynamic = True
+        return lin
+
     def slot_ptr(self) -> int:
         return N.slot_ptr(self.slots, self.slot)
 

@@ -176,3 +176,23 @@ def test_attention_block_sparse_config_mask():
     got = to_np(A.fp8(*(to_dev(t)[None] for t in (q, k, v)), mask=m)[0])
     device_ok()
     assert OO.cosine(got, OO.sdpa(q, k, v, tile_lists=m.lists)) >= 0.998
+
+
+def test_fp4attn_interface():
+    """tfvideo.fp4attn.attention keeps the reference's signature (tfvideo/fp4attn.py:245-246): qk/pv "fp8" run the
+    B200 kernel, "fp4" raises ValueError, ``out`` is written in place."""
+
+    from tfvideo import attention as A
+    from tfvideo import fp4attn
+
+    S, H = 300, 2
+    q, k, v = (to_dev(_normed(H, S, s))[None] for s in (31, 32, 33))
+    ref = A.fp8(q, k, v)
+    assert torch.equal(fp4attn.attention(q, k, v, qk="fp8", pv="fp8"), ref)
+    assert torch.equal(fp4attn.attention(q, k, v, qk="fp8h", pv="fp8", pv_f16=True, smooth=False), ref)
+    out = torch.empty(1, H, S, 128, dtype=torch.bfloat16, device="cuda")
+    assert fp4attn.attention(q, k, v, qk="fp8", out=out) is out and torch.equal(out, ref)
+    for bad in (dict(qk="fp4"), dict(pv="fp4"), dict(qk="int8")):
+        with pytest.raises(ValueError):
+            fp4attn.attention(q, k, v, **bad)
+    device_ok()
