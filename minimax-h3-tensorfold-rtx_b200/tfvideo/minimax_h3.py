@@ -199,6 +199,18 @@ class MiniMaxH3Engine:
         self._forwards = 0
         N.scales_begin(self.slots, False)
 
+    def replace_blocks(self, blocks: list[Block], lora_sig: str = "", slots: torch.Tensor | None = None) -> None:
+        """Swap in re-converted blocks (a LoRA set merged, or the base weights restored); the next forward starts a
+        new run with exact per-call scales."""
+
+        if len(blocks) != len(self.blocks) and self.blocks:
+            raise ValueError(f"replace_blocks: {len(blocks)} blocks for an engine of {len(self.blocks)}")
+        self.blocks = blocks
+        if slots is not None:
+            self.slots = slots
+        self.lora_sig = lora_sig
+        self.end_run()
+
     def release_vram(self):
         self._buf = None
         torch.cuda.empty_cache()
