@@ -299,9 +299,11 @@ __host__ __device__ __forceinline__ size_t sf_tiled_offset(size_t r, size_t k16,
   return ((r >> 7) * (kgroups >> 2) + (k16 >> 2)) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (k16 & 3);
 }
 
-// atomicMax on a non-negative float stored in a 32-bit word (int ordering equals float ordering for >= 0).
+// atomicMax on a non-negative float stored in a 32-bit word (int ordering equals float ordering for >= 0).  The
+// word only grows, so a value that does not exceed what is already there is dropped after a plain read: tens of
+// thousands of warps updating one scale slot would otherwise serialise on that address.
 __device__ __forceinline__ void atomic_max_pos(float* addr, float v) {
-  atomicMax(reinterpret_cast<int*>(addr), __float_as_int(v));
+  if (v > *reinterpret_cast<volatile float*>(addr)) atomicMax(reinterpret_cast<int*>(addr), __float_as_int(v));
 }
 
 __device__ __forceinline__ float warp_max(float v) {
