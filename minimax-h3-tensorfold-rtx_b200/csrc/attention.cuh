@@ -171,100 +171,110 @@ __global__ void attn_stats_reduce_kernel(const float* ksum_part, const float* vm
   vinv[i] = __fdiv_rn(448.0f, vm);
 }
 
-// Per (128-token block, head), thread = token: Q row -> e4m3 [H][SP][128] + fp32 scale [H][SP]; K row (smoothed) ->
-// e4m3 with one scale per block [H][SP/128]; V -> e4m3 transposed [H][128][SP] (keys contiguous, the K-major B operand
-// of PV).  Rows t >= S are written as zeros.
+// Per (128-token block, head): Q row -> e4m3 [H][SP][128] + fp32 scale [H][SP]; K row (smoothed) -> e4m3 with one
+// scale per block [H][SP/128]; V -> e4m3 transposed [H][128][SP] (keys contiguous, the K-major B operand of PV).  Rows
+// t >= S are written as zeros.  Warp w takes rows 32 w .. 32 w + 31, one row at a time across its lanes (lane l owns
+// dims 4 l .. 4 l + 3), so every load is one 256-byte row and every e4m3 store one 128-byte row.  K is read twice (its
+// block max first; the second read comes from L2).  V goes through a shared-memory tile [d][t] four tokens at a time,
+// then leaves as 128-byte rows of the transpose.
 __global__ void __launch_bounds__(128) attn_quant_kernel(AttnView a, int S, int SP, int H, const float* kmean,
                                                          const float* vinv, uint8_t* q8, float* qscale, uint8_t* k8,
                                                          float* kscale, uint8_t* vt8) {
   __shared__ float red[4];
+  __shared__ uint32_t vt[128][33];   // [d][t / 4] words of e4m3 V (byte t % 4), padded
   const int blk = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
-  const int t = blk * 128 + tid;
-  const bool live = t < S;
-  const long long base = (long long)t * a.ld + (long long)h * a.hstride;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int d0 = lane * 4;
   const float qmul = kLog2e / sqrtf(128.0f);
-  uint32_t outw[32];
-  // ---- Q
-  {
+  auto row_ptr = [&](const __nv_bfloat16* base, int t) {
+    return reinterpret_cast<const uint2*>(base + (long long)t * a.ld + (long long)h * a.hstride + d0);
+  };
+  auto load4 = [&](const __nv_bfloat16* base, int t, float (&x)[4]) {
+    const uint2 u = t < S ? *row_ptr(base, t) : make_uint2(0, 0);
+    x[0] = bf16_lo(u.x);
+    x[1] = bf16_hi(u.x);
+    x[2] = bf16_lo(u.y);
+    x[3] = bf16_hi(u.y);
+  };
+  auto pack4 = [](const float (&y)[4], float inv) {
+    return e4m3x2(__fmul_rn(y[0], inv), __fmul_rn(y[1], inv)) |
+           (e4m3x2(__fmul_rn(y[2], inv), __fmul_rn(y[3], inv)) << 16);
+  };
+  // ---- Q: one fp32 scale per row
+#pragma unroll 4
+  for (int i = 0; i < 32; ++i) {
+    const int t = blk * 128 + warp * 32 + i;
+    float x[4];
+    load4(a.q, t, x);
     float amax = 0.f;
-    float x[128];
 #pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      uint4 u = live ? *reinterpret_cast<const uint4*>(a.q + base + c * 8) : make_uint4(0, 0, 0, 0);
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        x[c * 8 + 2 * j] = __fmul_rn(bf16_lo(w[j]), qmul);
-        x[c * 8 + 2 * j + 1] = __fmul_rn(bf16_hi(w[j]), qmul);
-      }
+    for (int j = 0; j < 4; ++j) {
+      x[j] = __fmul_rn(x[j], qmul);
+      amax = fmaxf(amax, fabsf(x[j]));
     }
-#pragma unroll
-    for (int i = 0; i < 128; ++i) amax = fmaxf(amax, fabsf(x[i]));
-    const float qr = __fdiv_rn(fmaxf(amax, 1e-30f), 448.0f);
-    const float inv = __fdiv_rn(1.0f, qr);
-#pragma unroll
-    for (int w = 0; w < 32; ++w)
-      outw[w] = e4m3x2(__fmul_rn(x[4 * w], inv), __fmul_rn(x[4 * w + 1], inv)) |
-                (e4m3x2(__fmul_rn(x[4 * w + 2], inv), __fmul_rn(x[4 * w + 3], inv)) << 16);
-    uint4* dst = reinterpret_cast<uint4*>(q8 + ((size_t)h * SP + t) * 128);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) dst[c] = make_uint4(outw[4 * c], outw[4 * c + 1], outw[4 * c + 2], outw[4 * c + 3]);
-    qscale[(size_t)h * SP + t] = qr;   // tiny but finite for padded rows: no NaN from masked keys
-  }
-  // ---- K (smoothed, one scale per 128-key block)
-  {
-    float x[128];
-    float amax = 0.f;
-    const float* km = kmean + h * 128;
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      uint4 u = live ? *reinterpret_cast<const uint4*>(a.k + base + c * 8) : make_uint4(0, 0, 0, 0);
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int d = c * 8 + 2 * j;
-        x[d] = live ? __fsub_rn(bf16_lo(w[j]), km[d]) : 0.f;
-        x[d + 1] = live ? __fsub_rn(bf16_hi(w[j]), km[d + 1]) : 0.f;
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < 128; ++i) amax = fmaxf(amax, fabsf(x[i]));
     amax = warp_max(amax);
-    if ((tid & 31) == 0) red[tid >> 5] = amax;
-    __syncthreads();
-    amax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-    const float kr = __fdiv_rn(fmaxf(amax, 1e-30f), 448.0f);
-    const float inv = __fdiv_rn(1.0f, kr);
-#pragma unroll
-    for (int w = 0; w < 32; ++w)
-      outw[w] = e4m3x2(__fmul_rn(x[4 * w], inv), __fmul_rn(x[4 * w + 1], inv)) |
-                (e4m3x2(__fmul_rn(x[4 * w + 2], inv), __fmul_rn(x[4 * w + 3], inv)) << 16);
-    uint4* dst = reinterpret_cast<uint4*>(k8 + ((size_t)h * SP + t) * 128);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) dst[c] = make_uint4(outw[4 * c], outw[4 * c + 1], outw[4 * c + 2], outw[4 * c + 3]);
-    if (tid == 0) kscale[(size_t)h * (SP / 128) + blk] = kr;
+    const float qr = __fdiv_rn(fmaxf(amax, 1e-30f), 448.0f);
+    const uint32_t w = pack4(x, __fdiv_rn(1.0f, qr));
+    reinterpret_cast<uint32_t*>(q8 + ((size_t)h * SP + t) * 128)[lane] = w;
+    if (lane == 0) qscale[(size_t)h * SP + t] = qr;   // tiny but finite for padded rows: no NaN from masked keys
   }
-  // ---- V (per channel), transposed through shared memory: thread t writes column t of the [128 d][128 t] tile,
-  // then each thread stores one row d with 16-byte writes
-  {
-    __shared__ uint32_t vt[128][33];   // [d][t / 4] words, padded
-    const float* vi = vinv + h * 128;
+  // ---- K (smoothed by the sequence mean, one scale per 128-key block)
+  float km[4];
 #pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      uint4 u = live ? *reinterpret_cast<const uint4*>(a.v + base + c * 8) : make_uint4(0, 0, 0, 0);
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  for (int j = 0; j < 4; ++j) km[j] = kmean[h * 128 + d0 + j];
+  auto smooth = [&](int t, float (&x)[4]) {
+    load4(a.k, t, x);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int d = c * 8 + 2 * j;
-        const uint32_t b = e4m3x2(__fmul_rn(bf16_lo(w[j]), vi[d]), __fmul_rn(bf16_hi(w[j]), vi[d + 1]));
-        reinterpret_cast<uint8_t*>(&vt[d][0])[tid] = (uint8_t)(b & 0xFF);
-        reinterpret_cast<uint8_t*>(&vt[d + 1][0])[tid] = (uint8_t)(b >> 8);
-      }
+    for (int j = 0; j < 4; ++j) x[j] = t < S ? __fsub_rn(x[j], km[j]) : 0.f;
+  };
+  float kmax = 0.f;
+#pragma unroll 4
+  for (int i = 0; i < 32; ++i) {
+    float x[4];
+    smooth(blk * 128 + warp * 32 + i, x);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) kmax = fmaxf(kmax, fabsf(x[j]));
+  }
+  kmax = warp_max(kmax);
+  if (lane == 0) red[warp] = kmax;
+  __syncthreads();
+  kmax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  const float kr = __fdiv_rn(fmaxf(kmax, 1e-30f), 448.0f);
+  const float kinv = __fdiv_rn(1.0f, kr);
+#pragma unroll 4
+  for (int i = 0; i < 32; ++i) {
+    const int t = blk * 128 + warp * 32 + i;
+    float x[4];
+    smooth(t, x);
+    reinterpret_cast<uint32_t*>(k8 + ((size_t)h * SP + t) * 128)[lane] = pack4(x, kinv);
+  }
+  if (tid == 0) kscale[(size_t)h * (SP / 128) + blk] = kr;
+  // ---- V (per channel), transposed: four tokens at a time into the [d][t] tile, then 128-byte rows out
+  float vi[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) vi[j] = vinv[h * 128 + d0 + j];
+#pragma unroll 2
+  for (int i = 0; i < 32; i += 4) {
+    uint32_t bytes[4] = {0u, 0u, 0u, 0u};   // dim d0 + j of tokens i .. i + 3, byte k for token i + k
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float x[4];
+      load4(a.v, blk * 128 + warp * 32 + i + k, x);
+      const uint32_t lo = e4m3x2(__fmul_rn(x[0], vi[0]), __fmul_rn(x[1], vi[1]));
+      const uint32_t hi = e4m3x2(__fmul_rn(x[2], vi[2]), __fmul_rn(x[3], vi[3]));
+      bytes[0] |= (lo & 0xFFu) << (8 * k);
+      bytes[1] |= (lo >> 8) << (8 * k);
+      bytes[2] |= (hi & 0xFFu) << (8 * k);
+      bytes[3] |= (hi >> 8) << (8 * k);
     }
-    __syncthreads();
-    uint4* dst = reinterpret_cast<uint4*>(vt8 + ((size_t)h * 128 + tid) * SP + (size_t)blk * 128);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) dst[k] = make_uint4(vt[tid][4 * k], vt[tid][4 * k + 1], vt[tid][4 * k + 2], vt[tid][4 * k + 3]);
+    for (int j = 0; j < 4; ++j) vt[d0 + j][(warp * 32 + i) / 4] = bytes[j];
+  }
+  __syncthreads();
+#pragma unroll 4
+  for (int r = 0; r < 32; ++r) {
+    const int d = warp * 32 + r;
+    reinterpret_cast<uint32_t*>(vt8 + ((size_t)h * 128 + d) * SP + (size_t)blk * 128)[lane] = vt[d][lane];
   }
 }
 
