@@ -6,8 +6,8 @@
 // (tfvideo/kernels.py:66-84, tfvideo/linear.py:219-233).
 //
 // CTA tile 128 x BN (BN = 256 or 128), K tile 256 elements (128 bytes, one 128-byte swizzle row), 4-stage smem ring.
-// Warp 0: TMA producer.  Warp 1: TMEM owner and MMA issuer (one thread).  Warps 2-9: epilogue, warp w reading TMEM
-// lanes 32 * (w % 4) .. +31 (one output row per thread) and half (w - 2) / 4 of the columns.  Persistent over tiles.
+// Warp 0: TMA producer.  Warp 1: TMEM owner and MMA issuer (one thread).  Warps 2..: epilogue, warp w reading TMEM
+// lanes 32 * (w % 4) .. +31 (one output row per thread) and share (w - 2) / 4 of the columns.  Persistent over tiles.
 #pragma once
 
 #include "common.cuh"
@@ -37,7 +37,11 @@ struct GemmArgs {
 };
 
 constexpr int kGemmStages = 4;
-constexpr int kGemmThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue (two per TMEM lane quadrant)
+// Warp 0 TMA, warp 1 MMA, then the epilogue warps: kGemmEpiWarps(EPI) per TMEM lane quadrant.  The activation
+// epilogues (GELU / SwiGLU + NVFP4 requantisation) do several times the arithmetic of the others per element and
+// take four, so that one tile's epilogue stays shorter than the next tile's mainloop.
+__host__ __device__ constexpr int kGemmEpiWarps(int epi) { return (epi == H3_EPI_ACT_Q || epi == H3_EPI_ACT_BF16) ? 4 : 2; }
+__host__ __device__ constexpr int kGemmThreads(int epi) { return 64 + 128 * kGemmEpiWarps(epi); }
 
 template <int BN>
 struct GemmSmem {
@@ -90,10 +94,12 @@ __device__ __forceinline__ void chunk_words(const uint32_t (&hold)[N], int c, ui
 }
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kGemmThreads(EPI), 1)
     gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const GemmArgs p) {
   using L = GemmSmem<BN>;
+  constexpr int EW = kGemmEpiWarps(EPI);   // epilogue warps per lane quadrant
+  constexpr int CW = BN / EW;              // columns of one epilogue thread
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
@@ -114,7 +120,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 8);
+    mbar_init(acc_empty, 4 * EW);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -193,7 +199,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;
-    const int cofs = ((warp - 2) >> 2) * (BN / 2);   // this warp's half of the tile's columns
+    const int cofs = ((warp - 2) >> 2) * CW;   // this warp's share of the tile's columns
     const float alpha = p.a_slot->act * p.g_b;
     const float inv_q = EPI == H3_EPI_ACT_Q ? __fdiv_rn(1.0f, p.q_slot->act) : 0.f;
     const int F = p.act_kind ? (p.N >> 1) : p.N;   // activation width (ACT_*)
@@ -210,15 +216,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         xrow = p.x + (size_t)row * p.ldx + n0 + cofs;
         gate = p.mod + ((size_t)p.idx[row] * 6 + 3 * p.gate_part + 2) * p.N + n0 + cofs;
 #pragma unroll
-        for (int b = 0; b < BN; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"((const char*)xrow + b));
+        for (int b = 0; b < 2 * CW; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"((const char*)xrow + b));
       }
       const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, ti & 1, 103));   // tcgen05.ld is warp-wide
       if (!ok) break;
       tc_fence_after();
       // phase 1: accumulator -> bf16(acc * gA * gB + bias) in registers, then TMEM goes back to the MMA warp
-      uint32_t hold[BN / 4];
+      uint32_t hold[CW / 2];
 #pragma unroll
-      for (int c = 0; c < BN / 64; ++c) {
+      for (int c = 0; c < CW / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + cofs + c * 32, r);
         tmem_ld_wait();
@@ -238,7 +244,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!live) continue;
       // phase 2: the global-memory half, overlapping the next tile's mainloop
 #pragma unroll 1
-      for (int c = 0; c < BN / 64; ++c) {
+      for (int c = 0; c < CW / 32; ++c) {
         const int nc = n0 + cofs + c * 32;
         uint32_t y[16];   // 32 bf16 values, columns nc..nc+31
         chunk_words(hold, c, y);

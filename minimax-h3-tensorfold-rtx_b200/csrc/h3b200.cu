@@ -109,7 +109,7 @@ template <int BN, int EPI>
 int launch_gemm_t(int grid, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& p, cudaStream_t st) {
   int rc = smem_optin(gemm_nvfp4_kernel<BN, EPI>, GemmSmem<BN>::TOTAL, &g_optin_gemm[BN == 256][EPI], "h3_gemm_nvfp4");
   if (rc) return rc;
-  gemm_nvfp4_kernel<BN, EPI><<<grid, kGemmThreads, GemmSmem<BN>::TOTAL, st>>>(ta, tb, p);
+  gemm_nvfp4_kernel<BN, EPI><<<grid, kGemmThreads(EPI), GemmSmem<BN>::TOTAL, st>>>(ta, tb, p);
   return H3_OK;
 }
 
