@@ -37,10 +37,11 @@ struct QkNormArgs {
 
 // One warp per token: its RoPE matrices are loaded once into registers (lane l's dims 4l..4l+3 need pairs 4l..4l+3
 // when they lie in the first half of the rotated span, 4l - rot/2.. in the second) and applied to the token's 2H head
-// rows, two rows in flight at a time.
-__device__ __forceinline__ void qk_row(__nv_bfloat16* row, const float* w, const float (&f)[4][4], int lane, int half,
-                                       int rot, int src, float eps) {
-  uint2 u = *reinterpret_cast<const uint2*>(row + lane * 4);
+// rows.  Rows go in groups of eight (q and k of four heads), all eight loaded before any is written back: the rows
+// live in one buffer, so a load placed after a store could not be moved ahead of it, and one row in flight at a time
+// leaves the HBM pipe mostly idle.
+__device__ __forceinline__ uint2 qk_row(uint2 u, const float* w, const float (&f)[4][4], int lane, int half, int rot,
+                                        int src, float eps) {
   float x[4] = {bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y)};
   float ss = 0.f;
 #pragma unroll
@@ -65,7 +66,7 @@ __device__ __forceinline__ void qk_row(__nv_bfloat16* row, const float* w, const
     else
       o[e] = y[e];
   }
-  *reinterpret_cast<uint2*>(row + lane * 4) = make_uint2(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]));
+  return make_uint2(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]));
 }
 
 __global__ void __launch_bounds__(256) qknorm_rope_kernel(QkNormArgs a) {
@@ -95,12 +96,24 @@ __global__ void __launch_bounds__(256) qknorm_rope_kernel(QkNormArgs a) {
     qw[e] = a.qw[d0 + e];
     kw[e] = a.kw[d0 + e];
   }
-  __nv_bfloat16* qrow = a.q + (long long)s * a.ld;
-  __nv_bfloat16* krow = a.k + (long long)s * a.ld;
-#pragma unroll 2
-  for (int h = 0; h < a.H; ++h) {
-    qk_row(qrow + h * 128, qw, f, lane, half, a.rot, src, a.eps);
-    qk_row(krow + h * 128, kw, f, lane, half, a.rot, src, a.eps);
+  __nv_bfloat16* qrow = a.q + (long long)s * a.ld + d0;
+  __nv_bfloat16* krow = a.k + (long long)s * a.ld + d0;
+  for (int h0 = 0; h0 < a.H; h0 += 4) {
+    uint2 u[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (h0 + j < a.H) {
+        u[2 * j] = *reinterpret_cast<const uint2*>(qrow + (h0 + j) * 128);
+        u[2 * j + 1] = *reinterpret_cast<const uint2*>(krow + (h0 + j) * 128);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (h0 + j < a.H) {
+        *reinterpret_cast<uint2*>(qrow + (h0 + j) * 128) = qk_row(u[2 * j], qw, f, lane, half, a.rot, src, a.eps);
+        *reinterpret_cast<uint2*>(krow + (h0 + j) * 128) = qk_row(u[2 * j + 1], kw, f, lane, half, a.rot, src, a.eps);
+      }
+    }
   }
 }
 
