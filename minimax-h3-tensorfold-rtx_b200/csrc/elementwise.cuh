@@ -55,6 +55,9 @@ __global__ void scales_begin_kernel(H3ScaleSlot* s, int n, int delayed, int* cli
 // squares is accumulated per lane chunk by chunk (rounded product, rounded sum) and combined by an xor butterfly,
 // so every lane holds the same bits; 1 / sqrt is an IEEE sqrt and an IEEE division.  oracle/ops.py:norm_mod states
 // the same order, which makes the output (and the NVFP4 codes of it) bit-reproducible on the CPU.
+// The row is read twice, once for the sum of squares and once for the transform; the second read hits L1 / L2.
+// Holding the row in registers between the passes instead (80 registers a lane at D = 5120) left four warps per SM
+// sub-partition, too few to cover the quantiser's dependent chains: 429 us against 253 us at S = 37,760.
 struct NormModArgs {
   const __nv_bfloat16* x;
   int ldx;
@@ -71,22 +74,19 @@ struct NormModArgs {
   H3ScaleSlot* slot;      // nullable: amax of y is accumulated here; act is the quantiser's global scale
 };
 
-template <int MAXIT>
 __global__ void __launch_bounds__(256) norm_mod_kernel(NormModArgs a) {
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= a.S) return;
   const int nit = (a.D + 255) >> 8;
   const __nv_bfloat16* xr = a.x + (size_t)row * a.ldx;
-  uint4 raw[MAXIT];
   float ss = 0.f;
-#pragma unroll
-  for (int it = 0; it < MAXIT; ++it) {
+#pragma unroll 4
+  for (int it = 0; it < nit; ++it) {
     int c = it * 256 + lane * 8;
-    raw[it] = make_uint4(0, 0, 0, 0);
-    if (it < nit && c < a.D) {
-      raw[it] = *reinterpret_cast<const uint4*>(xr + c);
-      const uint32_t* w = &raw[it].x;
+    if (c < a.D) {
+      const uint4 u = *reinterpret_cast<const uint4*>(xr + c);
+      const uint32_t* w = &u.x;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         float lo = bf16_lo(w[j]), hi = bf16_hi(w[j]);
@@ -107,13 +107,14 @@ __global__ void __launch_bounds__(256) norm_mod_kernel(NormModArgs a) {
   float amax = 0.f;
   const int kgroups = a.D >> 4;
   const bool sf_words = (kgroups & 3) == 0;   // every 4-group quad lies inside the row
-#pragma unroll
-  for (int it = 0; it < MAXIT; ++it) {
+#pragma unroll 1
+  for (int it = 0; it < nit; ++it) {
     int c = it * 256 + lane * 8;
-    bool ok = it < nit && c < a.D;
+    bool ok = c < a.D;
     float y[8];
     if (ok) {
-      const uint32_t* wv = &raw[it].x;
+      const uint4 u = *reinterpret_cast<const uint4*>(xr + c);
+      const uint32_t* wv = &u.x;
       float4 w0 = *reinterpret_cast<const float4*>(a.w + c), w1 = *reinterpret_cast<const float4*>(a.w + c + 4);
       float4 s0 = *reinterpret_cast<const float4*>(scale + c), s1 = *reinterpret_cast<const float4*>(scale + c + 4);
       float4 h0 = *reinterpret_cast<const float4*>(shift + c), h1 = *reinterpret_cast<const float4*>(shift + c + 4);

@@ -228,10 +228,7 @@ int h3_norm_mod(const void* x, int ldx, const float* w, const float* mod, const 
                 reinterpret_cast<__nv_bfloat16*>(out), ldo, codes, sf, sf_tiled, slot};
   const int rows_per_block = 8;
   const dim3 grid((S + rows_per_block - 1) / rows_per_block), block(32 * rows_per_block);
-  if (D <= 20 * 256)   // a row in registers: 16 bytes per lane per 256 columns
-    norm_mod_kernel<20><<<grid, block, 0, S_(stream)>>>(a);
-  else
-    norm_mod_kernel<24><<<grid, block, 0, S_(stream)>>>(a);
+  norm_mod_kernel<<<grid, block, 0, S_(stream)>>>(a);
   return check_launch("h3_norm_mod");
 }
 
