@@ -300,35 +300,37 @@ struct AttnArgs {
   long long ldo;
   int S, SP, H;
   // Block-sparse mask (NULL = dense): the KV tiles query tile qt attends to are kv_idx[kv_ptr[qt] .. kv_ptr[qt+1]),
-  // 128-token tiles, shared by all heads.  Sparse launches take one query tile per CTA.
+  // 128-token tiles, shared by all heads.  Sparse launches take one query tile per CTA (NT = 1).
   const int* kv_ptr;
   const int* kv_idx;
 };
 
-constexpr int kAttnStages = 4;
-// One CTA = two 128-row query tiles (A, B) of one head.  Each 128-key KV tile is taken in two 64-key halves, and each
-// query tile has two 64-column S buffers in TMEM (one per half), so QK^T of the next half runs on the tensor cores
-// while the softmax of this one does: a group of MMAs takes several hundred cycles from issue to its commit, which
-// then never sits in series with the softmax.  Warps 0-3: softmax of tile A, warps 4-7: tile B -- warp w on TMEM lane
-// quadrant w % 4, one thread per query row, so the row max needs no exchange between threads; warp 8: TMA; warps 9,
-// 10: MMA of tiles A, B (an issuing thread that stops at a barrier lets the tensor pipe run dry; two keep it fed).
-// TMEM columns: S_A [0, 64) and [64, 128), S_B [128, 192) and [192, 256), O_A [256, 384), O_B [384, 512); P of keys
-// 32c..32c+31 of a half (e4m3) is written over columns 32c..32c+7 of its S buffer.
-constexpr int kAttnThreads = 352;
-constexpr int kProdWarp = 8, kMmaWarp = 9;   // MMA warps kMmaWarp + tile
+// One CTA = NT 128-row query tiles (A, B) of one head: NT = 2 for dense launches; NT = 1 for block-sparse ones,
+// whose query tiles each walk their own KV list, and which then run two CTAs per SM, so that every SM sub-partition
+// still holds two softmax warps.  Each 128-key KV tile is taken in two 64-key halves, and each query tile has two
+// 64-column S buffers in TMEM (one per half), so QK^T of the next half runs on the tensor cores while the softmax of
+// this one does: a group of MMAs takes several hundred cycles from issue to its commit, which then never sits in
+// series with the softmax.  Warps 0-3: softmax of tile A, warps 4-7: tile B -- warp w on TMEM lane quadrant w % 4,
+// one thread per query row, so the row max needs no exchange between threads; warp 4 NT: TMA; warps 4 NT + 1 + t:
+// MMA of tile t (an issuing thread that stops at a barrier lets the tensor pipe run dry; two keep it fed).
+// TMEM columns (NT = 2): S_A [0, 64) and [64, 128), S_B [128, 192) and [192, 256), O_A [256, 384), O_B [384, 512);
+// (NT = 1): S_A [0, 128), O_A [128, 256).  P of keys 32c..32c+31 of a half (e4m3) is written over columns
+// 32c..32c+7 of its S buffer.
 constexpr int kQTile = 128;
-constexpr int kQPerCta = 2 * kQTile;
+__host__ __device__ constexpr int attn_stages(int nt) { return nt == 2 ? 4 : 2; }    // K/V smem ring depth
+__host__ __device__ constexpr int attn_threads(int nt) { return 160 * nt + 32; }   // 5 warps a tile + TMA warp
 constexpr float kTau = 2.0f;        // running-max lag allowed before O is rescaled (log2 units)
 constexpr float kPOffset = 8.807354922057604f - kTau;   // log2(448) - tau
 // Pairs of each 32-key chunk whose exp2 runs as a polynomial on the FMA pipe instead of the MUFU (bit i: keys 2i,
 // 2i + 1).  The MUFU completes 16 ex2 per cycle per SM, which alone would bound an FP8 tile's softmax at twice the
 // tile's MMA time; moving part of the exponentials to the FMA pipe shortens it.
 constexpr uint32_t kPolyPairs = 0x5252u;
+template <int NT>
 struct AttnSmem {
   static constexpr int TILE = 128 * 128;
   static constexpr int Q_OFF = 0;                                      // Q tiles A, B
-  static constexpr int KV_OFF = 2 * TILE;                               // per stage: K, V^T
-  static constexpr int KSC_OFF = KV_OFF + kAttnStages * 2 * TILE;       // this head's K-block scales
+  static constexpr int KV_OFF = NT * TILE;                              // per stage: K, V^T
+  static constexpr int KSC_OFF = KV_OFF + attn_stages(NT) * 2 * TILE;   // this head's K-block scales
   static constexpr int MAX_KBLK = 2048;                                 // sequences up to 262,144 tokens
   static constexpr int KVT_OFF = KSC_OFF + MAX_KBLK * 4;                // KV tile of each step (block-sparse)
   static constexpr int BAR_OFF = KVT_OFF + MAX_KBLK * 4;
@@ -433,10 +435,14 @@ __device__ __forceinline__ void mask_chunk(uint32_t (&s)[32], int valid) {
     if (e >= valid) s[e] = __float_as_uint(-INFINITY);
 }
 
-__global__ void __launch_bounds__(kAttnThreads, 1)
+template <int NT>
+__global__ void __launch_bounds__(attn_threads(NT), 3 - NT)
     attn_fp8_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnArgs p) {
-  using L = AttnSmem;
+  using L = AttnSmem<NT>;
+  constexpr int kAttnStages = attn_stages(NT);
+  constexpr int kProdWarp = 4 * NT, kMmaWarp = 4 * NT + 1;   // MMA warps kMmaWarp + tile
+  constexpr uint32_t kTmemCols = 256 * NT, kOCol = 128 * NT;  // O of tile t at column kOCol + 128 t
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
@@ -454,8 +460,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y;
   const bool sparse = p.kv_ptr != nullptr;
-  const int q0 = blockIdx.x * (sparse ? kQTile : kQPerCta);
-  const bool has_b = !sparse && q0 + kQTile < p.S;   // tile B holds queries of this sequence
+  const int q0 = blockIdx.x * NT * kQTile;
+  const bool has_b = NT == 2 && !sparse && q0 + kQTile < p.S;   // tile B holds queries of this sequence
   const int nkt = (p.S + 127) / 128;                  // KV tiles of the sequence
   // the CTA's KV steps: every KV tile in order (dense), or the query tile's list (block-sparse); step j reads KV tile
   // kvt_s[j] with K-block scale ksc_s[j].  An out-of-range list entry is recorded in the status word and skipped.
@@ -498,7 +504,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     fence_barrier_init();
   }
   if (warp == kMmaWarp) {
-    tmem_alloc(tmem_slot, 512);
+    tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -549,7 +555,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t vs = smem_u32(smem + L::KV_OFF + ((i >> 1) % kAttnStages) * 2 * L::TILE + L::TILE);
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb)
-          mma_fp8_ts(tmem + 256 + t * 128, tmem + t * 128 + hf * 64 + kb * 32,
+          mma_fp8_ts(tmem + kOCol + t * 128, tmem + t * 128 + hf * 64 + kb * 32,
                      sdesc_kmajor_sw128(vs + (2 * hf + kb) * 32), idesc_o, (i | kb) != 0);
       };
       // (a query tile with no KV tile -- an empty block-sparse row -- issues nothing; its output rows are zero)
@@ -588,7 +594,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int r = qd * 32 + lane;
     const int query = q0 + t * kQTile + r;
     const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
-    const uint32_t o_col = tmem + lane_off + 256 + t * 128;
+    const uint32_t o_col = tmem + lane_off + kOCol + t * 128;
     bool ok = t == 0 || has_b;
     const bool live = ok;
     const float qr = live ? p.qscale[(size_t)h * p.SP + query] : 0.f;
@@ -688,7 +694,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == kMmaWarp) tmem_dealloc(tmem, 512);
+  if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
 }
 
 }  // namespace h3

@@ -85,7 +85,7 @@ int smem_optin(K kernel, int bytes, unsigned* done_mask, const char* what) {
   return H3_OK;
 }
 
-unsigned g_optin_attn = 0;
+unsigned g_optin_attn[2] = {0, 0};   // [NT - 1]
 
 // Streaming multiprocessors of the current device (cached per device).
 int num_sms() {
@@ -368,9 +368,10 @@ int attn_run(const char* who, const void* q, const void* k, const void* v, long 
   if (!q || !k || !v || !out || !workspace) return fail(H3_ERR_ARG, "%s: NULL pointer", who);
   if (S <= 0 || H <= 0 || ld % 8 || hstride % 8 || ldo % 8)
     return fail(H3_ERR_SHAPE, "%s: need strides %% 8 == 0", who);
-  if (S > AttnSmem::MAX_KBLK * 128 || H > 65535)
-    return fail(H3_ERR_SHAPE, "%s: S=%d, H=%d beyond the supported S <= %d, H <= 65535", who, S, H,
-                AttnSmem::MAX_KBLK * 128);
+  constexpr int kMaxS = AttnSmem<2>::MAX_KBLK * 128;
+  static_assert(AttnSmem<1>::MAX_KBLK == AttnSmem<2>::MAX_KBLK, "one sequence limit");
+  if (S > kMaxS || H > 65535)
+    return fail(H3_ERR_SHAPE, "%s: S=%d, H=%d beyond the supported S <= %d, H <= 65535", who, S, H, kMaxS);
   if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16) || !aligned(workspace, 1024))
     return fail(H3_ERR_ARG, "%s: q/k/v/out 16-byte and workspace 1024-byte alignment required", who);
   AttnWs w = attn_ws(S, H);
@@ -401,11 +402,15 @@ int attn_run(const char* who, const void* q, const void* k, const void* v, long 
   if ((rc = make_map_u8(&tq, q8, 128, (uint64_t)H * w.SP, 128, 128, 128, who))) return rc;
   if ((rc = make_map_u8(&tk, k8, 128, (uint64_t)H * w.SP, 128, 128, 128, who))) return rc;
   if ((rc = make_map_u8(&tv, vt8, w.SP, (uint64_t)H * 128, w.SP, 128, 128, who))) return rc;
-  if ((rc = smem_optin(attn_fp8_kernel, AttnSmem::TOTAL, &g_optin_attn, who))) return rc;
   AttnArgs p{qscale, kscale, vscale, reinterpret_cast<__nv_bfloat16*>(out), ldo, S, w.SP, H, kv_ptr, kv_idx};
-  const int qtiles_per_cta = kv_ptr ? kQTile : kQPerCta;   // block-sparse launches take one query tile per CTA
-  attn_fp8_kernel<<<dim3((S + qtiles_per_cta - 1) / qtiles_per_cta, H), kAttnThreads, AttnSmem::TOTAL, st>>>(tq, tk,
-                                                                                                         tv, p);
+  if (kv_ptr) {   // block-sparse: one query tile per CTA (each has its own KV list), two CTAs per SM
+    if ((rc = smem_optin(attn_fp8_kernel<1>, AttnSmem<1>::TOTAL, &g_optin_attn[0], who))) return rc;
+    attn_fp8_kernel<1><<<dim3((S + kQTile - 1) / kQTile, H), attn_threads(1), AttnSmem<1>::TOTAL, st>>>(tq, tk, tv, p);
+  } else {
+    if ((rc = smem_optin(attn_fp8_kernel<2>, AttnSmem<2>::TOTAL, &g_optin_attn[1], who))) return rc;
+    attn_fp8_kernel<2><<<dim3((S + 2 * kQTile - 1) / (2 * kQTile), H), attn_threads(2), AttnSmem<2>::TOTAL, st>>>(
+        tq, tk, tv, p);
+  }
   return check_launch(who);
 }
 }  // namespace
