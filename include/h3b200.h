@@ -34,7 +34,8 @@ enum {
   H3_EPI_STORE = 0,       /* out = bf16(acc * gA * gB + bias) */
   H3_EPI_GATE_RESID = 1,  /* x = bf16(x + bf16(acc * gA * gB + bias) * gate[idx[row]]): gate_add fused */
   H3_EPI_ACT_BF16 = 2,    /* out = bf16(act(bf16(y))), amax of it into q_slot */
-  H3_EPI_ACT_Q = 3        /* act as above, quantised to NVFP4 under q_slot->act (and amax into q_slot) */
+  H3_EPI_ACT_Q = 3,       /* act as above, quantised to NVFP4 under q_slot->act (and amax into q_slot) */
+  H3_EPI_STORE_PEERS = 4  /* STORE, each head's columns into the receive buffer of the rank that owns the head */
 };
 
 /* Activation-scale state of one linear input (16 bytes, device memory).  amax: max |input| seen this forward
@@ -62,6 +63,15 @@ typedef struct H3Epilogue {
   uint8_t* qcodes;       /* ACT_Q: NVFP4 codes [M, F / 2] */
   uint8_t* qsf;          /* ACT_Q: tiled scales (see h3_sf_tiled_bytes) */
   H3ScaleSlot* q_slot;   /* ACT_*: the activation's scale slot */
+  /* STORE_PEERS (Ulysses sequence parallelism; no counterpart in the reference, which runs on one GPU): the GEMM's
+   * M rows are this rank's M tokens of qkv, N = 3 H 128.  Element (row, part, head, d) is stored to
+   * peer[head / Hr] at bf16 element ((rank * M + row) * 3 + part) * Hr * 128 + (head % Hr) * 128 + d, Hr = H / ranks:
+   * every rank's [ranks * M, 3, Hr, 128] receive buffer gets all tokens of its heads.  peer[r] is rank r's buffer as
+   * mapped in this process (h3_peer_alloc / h3_peer_open), or any base the rows for rank r are to be offset from
+   * (e.g. a local staging buffer that h3_peer_push then sends in contiguous blocks). */
+  void* peer[8];
+  int ranks;             /* 1..8; N % (3 * 128 * ranks) == 0 */
+  int rank;
 } H3Epilogue;
 
 /* ---------------------------------------------------------------------------------------------- library */
@@ -109,6 +119,26 @@ int h3_act(const void* u, int ldu, void* out, int ldo, int M, int F, int act_kin
 int h3_modulation(const float* t_emb, int M, int t_dim, const float* ada_w, const float* ada_b, int J, float* mod,
                   void* stream);
 
+/* ---------------------------------------------------------------------------------------------- peer memory */
+/* Device buffers other processes on the node map (CUDA IPC), the receive buffers of the fused Ulysses exchanges.
+ * No counterpart in the reference (one GPU).  h3_peer_alloc allocates `bytes` on the current device and writes its
+ * 64-byte IPC handle to `handle`; another process passes that handle to h3_peer_open to map the buffer (peer access
+ * enabled on demand).  Close mappings before the owner frees the buffer. */
+int h3_peer_alloc(size_t bytes, void** ptr, void* handle);
+int h3_peer_open(const void* handle, void** ptr);
+int h3_peer_close(void* ptr);
+int h3_peer_free(void* ptr);
+/* One contiguous device-to-device copy of h3_peer_push: src and dst 16-byte aligned, bytes a multiple of 16. */
+typedef struct H3PeerCopy {
+  const void* src;
+  void* dst;
+  size_t bytes;
+} H3PeerCopy;
+/* Up to 8 copies in one kernel, typically into other ranks' peer buffers: every warp stores 512 contiguous bytes at a
+ * time, so writes to another GPU cross NVLink in full packets (row-scattered 16-byte stores do not).  Like any
+ * kernel's, its writes are visible to work ordered after its completion (for another rank: after a barrier). */
+int h3_peer_push(const H3PeerCopy* copies, int n, void* stream);
+
 /* ---------------------------------------------------------------------------------------------- GEMM */
 /* NVFP4 W4A4 GEMM y = A x B^T (replaces Nvfp4Linear.__call__ -> TensorFold prompt(A4, x, lin),
  * tfvideo/linear.py:141-151): A codes [M, K/2] and tiled scales (h3_sf_tiled_bytes(M, K)) with global scale
@@ -144,6 +174,17 @@ int h3_attn_fp8(const void* q, const void* k, const void* v, long long ld, long 
 int h3_attn_fp8_sparse(const void* q, const void* k, const void* v, long long ld, long long hstride, int S, int H,
                        const int* kv_ptr, const int* kv_idx, void* out, long long ldo, void* workspace,
                        size_t workspace_bytes, void* stream);
+
+/* h3_attn_fp8 (kv_ptr NULL) or h3_attn_fp8_sparse whose output rows go straight to the ranks that own the tokens
+ * (Ulysses sequence parallelism; no counterpart in the reference, which runs on one GPU).  q, k, v hold all S tokens
+ * of this rank's H heads; the token t's row of head h goes to peer[t / n] (n = S / ranks) at bf16 element
+ * ((rank * n + t % n) * ldo + h * 128 + d): every rank's [ranks, n, ldo] receive buffer gets its n tokens, column
+ * block r from rank r's heads.  peer: host array of `ranks` (1..8) buffers as mapped in this process
+ * (h3_peer_alloc / h3_peer_open), or any base the rows for rank r are to be offset from (e.g. a local staging buffer
+ * that h3_peer_push then sends in contiguous blocks); S % ranks == 0. */
+int h3_attn_fp8_peers(const void* q, const void* k, const void* v, long long ld, long long hstride, int S, int H,
+                      const int* kv_ptr, const int* kv_idx, void* const* peer, int ranks, int rank, long long ldo,
+                      void* workspace, size_t workspace_bytes, void* stream);
 
 /* The same attention as h3_attn_fp8 for callers that cannot allocate device memory -- for example code running
  * inside a host framework that owns every device allocation (ComfyUI records and replays a block's allocations under

@@ -303,6 +303,10 @@ struct AttnArgs {
   // 128-token tiles, shared by all heads.  Sparse launches take one query tile per CTA (NT = 1).
   const int* kv_ptr;
   const int* kv_idx;
+  // Output to peers (ranks > 0, Ulysses): token t's row goes to peer[t / n_local] at row rank * n_local + t % n_local
+  // (row length ldo) instead of to out.
+  unsigned long long peer[8];
+  int ranks, rank, n_local;
 };
 
 // One CTA = NT 128-row query tiles (A, B) of one head: NT = 2 for dense launches; NT = 1 for block-sparse ones,
@@ -677,7 +681,16 @@ __global__ void __launch_bounds__(attn_threads(NT), 3 - NT)
         tmem_ld32(o_col + 32 * c, o);
         tmem_ld_wait();
         if (query < p.S) {
-          uint4* d4 = reinterpret_cast<uint4*>(p.out + (long long)query * p.ldo + h * 128 + 32 * c);
+          __nv_bfloat16* orow = p.out + (long long)query * p.ldo;
+          // to the token's owner's receive buffer (NVLink stores for other ranks' tokens).  No fence: whatever
+          // reads them is ordered after this kernel's completion (a barrier on every rank), and a completed kernel's
+          // writes, peer memory included, are visible to work ordered after it.
+          if (p.ranks > 0) {
+            const int owner = query / p.n_local;
+            orow = reinterpret_cast<__nv_bfloat16*>(p.peer[owner]) +
+                   (long long)(p.rank * p.n_local + query - owner * p.n_local) * p.ldo;
+          }
+          uint4* d4 = reinterpret_cast<uint4*>(orow + h * 128 + 32 * c);
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4) {
             float f[8];

@@ -34,6 +34,9 @@ struct GemmArgs {
   uint8_t* qcodes;               // ACT_Q: NVFP4 codes of the activation [M, F/2]
   uint8_t* qsf;                  // ACT_Q: tiled scales of the activation
   H3ScaleSlot* q_slot;           // ACT_BF16 / ACT_Q: amax of the activation; ACT_Q quantises under q_slot->act
+  // STORE_PEERS: the qkv rows of this rank's M tokens, each head's 128 columns to the rank owning the head
+  unsigned long long peer[8];
+  int ranks, rank;
 };
 
 constexpr int kGemmStages = 4;
@@ -248,8 +251,17 @@ __global__ void __launch_bounds__(kGemmThreads(EPI), 1)
         const int nc = n0 + cofs + c * 32;
         uint32_t y[16];   // 32 bf16 values, columns nc..nc+31
         chunk_words(hold, c, y);
-        if (EPI == H3_EPI_STORE) {
-          uint4* o = reinterpret_cast<uint4*>(p.out + (size_t)row * p.ldo + nc);
+        if (EPI == H3_EPI_STORE || EPI == H3_EPI_STORE_PEERS) {
+          __nv_bfloat16* dst = p.out + (size_t)row * p.ldo + nc;
+          if (EPI == H3_EPI_STORE_PEERS) {
+            // column nc = (part, head, d): a 32-column chunk lies inside one 128-column head
+            const int H = p.N / 384, Hr = H / p.ranks;
+            const int part = nc / (H * 128), head = (nc >> 7) - part * H, d = nc & 127;
+            const int owner = head / Hr;
+            dst = reinterpret_cast<__nv_bfloat16*>(p.peer[owner]) +
+                  ((size_t)((p.rank * p.M + row) * 3 + part) * Hr + (head - owner * Hr)) * 128 + d;
+          }
+          uint4* o = reinterpret_cast<uint4*>(dst);
 #pragma unroll
           for (int j = 0; j < 4; ++j) o[j] = make_uint4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
         } else if (EPI == H3_EPI_GATE_RESID) {

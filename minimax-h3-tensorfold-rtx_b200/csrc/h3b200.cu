@@ -103,7 +103,7 @@ int num_sms() {
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-unsigned g_optin_gemm[2][4] = {};
+unsigned g_optin_gemm[2][5] = {};
 
 template <int BN, int EPI>
 int launch_gemm_t(int grid, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& p, cudaStream_t st) {
@@ -115,15 +115,17 @@ int launch_gemm_t(int grid, const CUtensorMap& ta, const CUtensorMap& tb, const 
 
 int launch_gemm(int BN, int epi, int grid, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& p,
                 cudaStream_t st) {
-  switch (epi + 4 * (BN == 256)) {
+  switch (epi + 5 * (BN == 256)) {
     case 0: return launch_gemm_t<128, H3_EPI_STORE>(grid, ta, tb, p, st);
     case 1: return launch_gemm_t<128, H3_EPI_GATE_RESID>(grid, ta, tb, p, st);
     case 2: return launch_gemm_t<128, H3_EPI_ACT_BF16>(grid, ta, tb, p, st);
     case 3: return launch_gemm_t<128, H3_EPI_ACT_Q>(grid, ta, tb, p, st);
-    case 4: return launch_gemm_t<256, H3_EPI_STORE>(grid, ta, tb, p, st);
-    case 5: return launch_gemm_t<256, H3_EPI_GATE_RESID>(grid, ta, tb, p, st);
-    case 6: return launch_gemm_t<256, H3_EPI_ACT_BF16>(grid, ta, tb, p, st);
-    default: return launch_gemm_t<256, H3_EPI_ACT_Q>(grid, ta, tb, p, st);
+    case 4: return launch_gemm_t<128, H3_EPI_STORE_PEERS>(grid, ta, tb, p, st);
+    case 5: return launch_gemm_t<256, H3_EPI_STORE>(grid, ta, tb, p, st);
+    case 6: return launch_gemm_t<256, H3_EPI_GATE_RESID>(grid, ta, tb, p, st);
+    case 7: return launch_gemm_t<256, H3_EPI_ACT_BF16>(grid, ta, tb, p, st);
+    case 8: return launch_gemm_t<256, H3_EPI_ACT_Q>(grid, ta, tb, p, st);
+    default: return launch_gemm_t<256, H3_EPI_STORE_PEERS>(grid, ta, tb, p, st);
   }
 }
 
@@ -186,6 +188,92 @@ int h3_device_status(int* status, int reset) {
 size_t h3_sf_tiled_bytes(int rows, int cols) {
   if (rows <= 0 || cols <= 0) return 0;
   return (size_t)((rows + 127) / 128) * 128 * (size_t)(cols / 16);
+}
+
+// ------------------------------------------------------------------------------------------------ peer memory
+// Receive buffers of the fused Ulysses exchanges: plain cudaMalloc allocations shared through CUDA IPC handles
+// (no multicast object, no NVLS binding), mapped by the other ranks' processes.
+int h3_peer_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return fail(H3_ERR_ARG, "h3_peer_alloc: NULL argument or zero bytes");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "64-byte IPC handle");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return fail(H3_ERR_CUDA, "h3_peer_alloc: cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+  e = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(handle), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(H3_ERR_CUDA, "h3_peer_alloc: cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+  }
+  *ptr = p;
+  return H3_OK;
+}
+
+int h3_peer_open(const void* handle, void** ptr) {
+  if (!ptr || !handle) return fail(H3_ERR_ARG, "h3_peer_open: NULL argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(H3_ERR_CUDA, "h3_peer_open: cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+  return H3_OK;
+}
+
+int h3_peer_close(void* ptr) {
+  if (!ptr) return fail(H3_ERR_ARG, "h3_peer_close: NULL pointer");
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return fail(H3_ERR_CUDA, "h3_peer_close: %s", cudaGetErrorString(e));
+  return H3_OK;
+}
+
+namespace {
+struct PushArgs {
+  const uint4* src[8];
+  uint4* dst[8];
+  long long n16[8];   // 16-byte words of each copy
+};
+// blockIdx.y: the copy; grid-stride over its 16-byte words, four loads in flight per thread
+__global__ void __launch_bounds__(256) peer_push_kernel(const __grid_constant__ PushArgs a) {
+  const int c = blockIdx.y;
+  const uint4* __restrict__ src = a.src[c];
+  uint4* dst = a.dst[c];
+  const long long n = a.n16[c], step = (long long)gridDim.x * blockDim.x;
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + 3 * step < n; i += 4 * step) {
+    const uint4 v0 = src[i], v1 = src[i + step], v2 = src[i + 2 * step], v3 = src[i + 3 * step];
+    dst[i] = v0;
+    dst[i + step] = v1;
+    dst[i + 2 * step] = v2;
+    dst[i + 3 * step] = v3;
+  }
+  for (; i < n; i += step) dst[i] = src[i];
+}
+}  // namespace
+
+int h3_peer_push(const H3PeerCopy* copies, int n, void* stream) {
+  if (!copies || n < 1 || n > 8) return fail(H3_ERR_ARG, "h3_peer_push: need 1..8 copies (n=%d)", n);
+  PushArgs a{};
+  long long most = 0;
+  for (int c = 0; c < n; ++c) {
+    if (!copies[c].src || !copies[c].dst || !aligned(copies[c].src, 16) || !aligned(copies[c].dst, 16) ||
+        copies[c].bytes % 16)
+      return fail(H3_ERR_ARG, "h3_peer_push: copy %d needs 16-byte aligned src/dst and bytes %% 16 == 0", c);
+    a.src[c] = reinterpret_cast<const uint4*>(copies[c].src);
+    a.dst[c] = reinterpret_cast<uint4*>(copies[c].dst);
+    a.n16[c] = (long long)(copies[c].bytes / 16);
+    most = a.n16[c] > most ? a.n16[c] : most;
+  }
+  if (most == 0) return H3_OK;
+  long long blocks = (most + 1023) / 1024;
+  const long long cap = 2LL * num_sms();   // per copy; n copies share the SMs
+  if (blocks > cap) blocks = cap;
+  peer_push_kernel<<<dim3((unsigned)blocks, n), 256, 0, S_(stream)>>>(a);
+  return check_launch("h3_peer_push");
+}
+
+int h3_peer_free(void* ptr) {
+  if (!ptr) return fail(H3_ERR_ARG, "h3_peer_free: NULL pointer");
+  cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return fail(H3_ERR_CUDA, "h3_peer_free: %s", cudaGetErrorString(e));
+  return H3_OK;
 }
 
 // ------------------------------------------------------------------------------------------------ scales
@@ -313,6 +401,18 @@ int h3_gemm_nvfp4(const uint8_t* a_codes, const uint8_t* a_sf, const H3ScaleSlot
     case H3_EPI_STORE:
       if (!p.out || p.ldo % 8 || !aligned(p.out, 16)) return fail(H3_ERR_ARG, "h3_gemm_nvfp4: STORE needs out");
       break;
+    case H3_EPI_STORE_PEERS:
+      if (epi->ranks < 1 || epi->ranks > 8 || epi->rank < 0 || epi->rank >= epi->ranks || N % (384 * epi->ranks))
+        return fail(H3_ERR_ARG, "h3_gemm_nvfp4: STORE_PEERS needs 1 <= ranks <= 8, 0 <= rank < ranks and N a "
+                                "multiple of 3 * 128 * ranks (ranks=%d rank=%d N=%d)", epi->ranks, epi->rank, N);
+      for (int r = 0; r < epi->ranks; ++r) {
+        if (!epi->peer[r] || !aligned(epi->peer[r], 16))
+          return fail(H3_ERR_ARG, "h3_gemm_nvfp4: STORE_PEERS peer[%d] NULL or not 16-byte aligned", r);
+        p.peer[r] = reinterpret_cast<unsigned long long>(epi->peer[r]);
+      }
+      p.ranks = epi->ranks;
+      p.rank = epi->rank;
+      break;
     case H3_EPI_GATE_RESID:
       if (!p.x || !p.mod || !p.idx || p.ldx % 8 || !aligned(p.x, 16) || (p.gate_part != 0 && p.gate_part != 1))
         return fail(H3_ERR_ARG, "h3_gemm_nvfp4: GATE_RESID needs x, mod, idx, gate_part");
@@ -362,9 +462,23 @@ size_t h3_attn_workspace_bytes(int S, int H) {
 
 namespace {
 // Prepare (K mean / V max, FP8 quantisation) and the attention kernel, dense (kv_ptr NULL) or block-sparse.
+struct PeerOut {   // h3_attn_fp8_peers: output rows to the ranks that own the tokens
+  void* const* peer;
+  int ranks, rank;
+};
+
 int attn_run(const char* who, const void* q, const void* k, const void* v, long long ld, long long hstride, int S,
              int H, const int* kv_ptr, const int* kv_idx, void* out, long long ldo, void* workspace,
-             size_t workspace_bytes, void* stream) {
+             size_t workspace_bytes, void* stream, const PeerOut* po = nullptr) {
+  if (po) {
+    if (!po->peer || po->ranks < 1 || po->ranks > 8 || po->rank < 0 || po->rank >= po->ranks || S % po->ranks)
+      return fail(H3_ERR_ARG, "%s: need 1 <= ranks <= 8, 0 <= rank < ranks, S %% ranks == 0 (S=%d ranks=%d rank=%d)",
+                  who, S, po->ranks, po->rank);
+    for (int r = 0; r < po->ranks; ++r)
+      if (!po->peer[r] || !aligned(po->peer[r], 16)) return fail(H3_ERR_ARG, "%s: peer[%d] NULL or misaligned", who, r);
+    if (ldo < (long long)H * 128) return fail(H3_ERR_ARG, "%s: receive rows of %lld < H * 128 elements", who, ldo);
+    out = po->peer[po->rank];
+  }
   if (!q || !k || !v || !out || !workspace) return fail(H3_ERR_ARG, "%s: NULL pointer", who);
   if (S <= 0 || H <= 0 || ld % 8 || hstride % 8 || ldo % 8)
     return fail(H3_ERR_SHAPE, "%s: need strides %% 8 == 0", who);
@@ -403,6 +517,12 @@ int attn_run(const char* who, const void* q, const void* k, const void* v, long 
   if ((rc = make_map_u8(&tk, k8, 128, (uint64_t)H * w.SP, 128, 128, 128, who))) return rc;
   if ((rc = make_map_u8(&tv, vt8, w.SP, (uint64_t)H * 128, w.SP, 128, 128, who))) return rc;
   AttnArgs p{qscale, kscale, vscale, reinterpret_cast<__nv_bfloat16*>(out), ldo, S, w.SP, H, kv_ptr, kv_idx};
+  if (po) {
+    for (int r = 0; r < po->ranks; ++r) p.peer[r] = reinterpret_cast<unsigned long long>(po->peer[r]);
+    p.ranks = po->ranks;
+    p.rank = po->rank;
+    p.n_local = S / po->ranks;
+  }
   if (kv_ptr) {   // block-sparse: one query tile per CTA (each has its own KV list), two CTAs per SM
     if ((rc = smem_optin(attn_fp8_kernel<1>, AttnSmem<1>::TOTAL, &g_optin_attn[0], who))) return rc;
     attn_fp8_kernel<1><<<dim3((S + kQTile - 1) / kQTile, H), attn_threads(1), AttnSmem<1>::TOTAL, st>>>(tq, tk, tv, p);
@@ -419,6 +539,17 @@ int h3_attn_fp8(const void* q, const void* k, const void* v, long long ld, long 
                 long long ldo, void* workspace, size_t workspace_bytes, void* stream) {
   return attn_run("h3_attn_fp8", q, k, v, ld, hstride, S, H, nullptr, nullptr, out, ldo, workspace, workspace_bytes,
                   stream);
+}
+
+int h3_attn_fp8_peers(const void* q, const void* k, const void* v, long long ld, long long hstride, int S, int H,
+                      const int* kv_ptr, const int* kv_idx, void* const* peer, int ranks, int rank, long long ldo,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  if ((kv_ptr == nullptr) != (kv_idx == nullptr)) return fail(H3_ERR_ARG, "h3_attn_fp8_peers: half a tile list");
+  if (kv_ptr && (!aligned(kv_ptr, 4) || !aligned(kv_idx, 4)))
+    return fail(H3_ERR_ARG, "h3_attn_fp8_peers: misaligned tile list");
+  const PeerOut po{peer, ranks, rank};
+  return attn_run("h3_attn_fp8_peers", q, k, v, ld, hstride, S, H, kv_ptr, kv_idx, nullptr, ldo, workspace,
+                  workspace_bytes, stream, &po);
 }
 
 int h3_attn_fp8_sparse(const void* q, const void* k, const void* v, long long ld, long long hstride, int S, int H,

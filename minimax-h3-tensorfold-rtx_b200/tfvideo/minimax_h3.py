@@ -21,6 +21,7 @@ import os
 from dataclasses import dataclass, field
 
 import torch
+import torch.distributed as dist
 
 from . import attention as A
 from . import kernels as K
@@ -92,7 +93,7 @@ def synthetic_weights(cfg: Config, seed: int = 1, device="cuda"):
 class _Buffers:
     """Per-sequence-length activations and scratch (allocated once per shape, reused by every block)."""
 
-    def __init__(self, cfg: Config, n: int, S: int, world: int, M: int, device):
+    def __init__(self, cfg: Config, n: int, S: int, world: int, M: int, device, peers=None):
         D, HD, F = cfg.dim, cfg.inner, cfg.ffn
         e = dict(device=device)
         self.key = (n, S, M)
@@ -107,9 +108,14 @@ class _Buffers:
         self.a4 = torch.empty((n, F // 2), dtype=torch.uint8, **e)
         self.a4sf = torch.zeros(N.sf_tiled_bytes(n, F), dtype=torch.uint8, **e)
         self.mod = torch.empty((M, 18 * D), dtype=torch.float32, **e)
+        self.peers = None
         if world > 1:
-            self.qkv_all = torch.empty((S, 3, Hl, cfg.head_dim), dtype=torch.bfloat16, **e)
-            self.o_recv = torch.empty((world, n, Hl * cfg.head_dim), dtype=torch.bfloat16, **e)
+            if peers is not None:   # receive buffers the other ranks' kernels store into (fused exchanges)
+                self.peers = peers
+                self.qkv_all, self.o_recv = peers[0].tensor, peers[1].tensor
+            else:
+                self.qkv_all = torch.empty((S, 3, Hl, cfg.head_dim), dtype=torch.bfloat16, **e)
+                self.o_recv = torch.empty((world, n, Hl * cfg.head_dim), dtype=torch.bfloat16, **e)
         self._dyn = None
 
     def dynamic(self, cfg: Config, n: int, device):
@@ -250,8 +256,23 @@ class MiniMaxH3Engine:
         world = 1 if self.sp is None else self.sp.world
         if self._buf is None or self._buf.key != (n, S, M):
             self._buf = None
-            self._buf = _Buffers(self.cfg, n, S, world, M, self.device)
+            self._buf = _Buffers(self.cfg, n, S, world, M, self.device, self._peer_buffers(n, S))
         return self._buf
+
+    def _peer_buffers(self, n: int, S: int):
+        """The qkv and attention-output receive buffers of the fused Ulysses exchanges (NCCL groups on GPUs), made
+        once per sequence length: every rank maps every rank's, so they are kept rather than freed."""
+
+        if self.sp is None or self.device.type != "cuda" or dist.get_backend(self.sp.group) != "nccl":
+            return None
+        key = (n, S)
+        cache = self.__dict__.setdefault("_peer_cache", {})
+        if key not in cache:
+            from .parallel import PeerBuffer
+            Hl, Dh = self.cfg.heads // self.sp.world, self.cfg.head_dim
+            cache[key] = (PeerBuffer(self.sp, (S, 3, Hl, Dh), torch.bfloat16, self.device),
+                          PeerBuffer(self.sp, (self.sp.world, n, Hl * Dh), torch.bfloat16, self.device))
+        return cache[key]
 
     def _slot(self, i: int, name: str) -> int:
         return N.slot_ptr(self.slots, 4 * i + SLOT[name])
@@ -296,31 +317,67 @@ class MiniMaxH3Engine:
             else:
                 self._dynamic_scale(i, "qkv")
                 N.nvfp4_quant(h, buf.h4, buf.h4sf, g_ptr=self._slot(i, "qkv") + 4)
-        # ---- qkv, q/k RMSNorm + RoPE
-        with maybe(T, "gemm_qkv"):
-            lq.gemm(buf.h4, buf.h4sf, n, N.H3Epilogue(kind=N.H3_EPI_STORE, out=buf.qkv.data_ptr(), ldo=3 * HD))
-        rope = self.rope_table(rope_freqs, S)[t0:t0 + n]
-        rot = rope.shape[1] * 2
-        q, k, v = buf.qkv[:, :HD], buf.qkv[:, HD:2 * HD], buf.qkv[:, 2 * HD:]
-        with maybe(T, "qknorm_rope"):
-            N.qknorm_rope(q, k, 3 * HD, n, H, rot, b.q_norm, b.k_norm, rope, cfg.qk_eps)
-        # ---- attention
+        # ---- qkv, q/k RMSNorm + RoPE, attention
+        rope_all = self.rope_table(rope_freqs, S)
+        rot = rope_all.shape[1] * 2
         ws = A.aligned_workspace(buf.attn_ws)
-        if self.sp is None:
-            with maybe(T, "attention"):
-                self._attend(q, k, v, S, H, 3 * HD, buf.o, ws)
-            src = dict(x=buf.o, R=n, K=HD)
-        else:
-            Hl = H // world
-            with maybe(T, "all_to_all"):
-                self.sp.qkv_heads_from_tokens(buf.qkv.view(n, 3, H, Dh), buf.qkv_all)
+        if self.sp is not None and buf.peers is not None and self.attn is A.fp8:
+            # Ulysses with the exchanges in the producing kernels: the qkv GEMM's epilogue writes each head's columns
+            # in the receiving rank's row layout -- this rank's heads straight into its own receive buffer, the other
+            # ranks' into one contiguous block each of a local staging buffer, which one push kernel then streams
+            # into their receive buffers over NVLink (row-scattered stores from the epilogue itself would cross the
+            # link as 16-byte requests).  The attention kernel stores each token's output rows straight into the
+            # owner's buffer: those stores are few and spread over the kernel's run (staging and pushing them measured
+            # no faster).  A barrier after each replaces the all-to-all.  RMSNorm + RoPE run on the received rows
+            # (all S tokens, this rank's heads): the same per-(token, head) arithmetic as before the exchange.
+            Hl, rank = H // world, self.sp.rank
+            qp, op = buf.peers
+            blk = n * 3 * Hl * Dh                     # elements one rank sends another
+            send, es = buf.qkv.data_ptr(), buf.qkv.element_size()
+            epi = N.H3Epilogue(kind=N.H3_EPI_STORE_PEERS, ranks=world, rank=rank)
+            for r in range(world):   # base the rows for rank r are offset from (the kernel adds rank * n rows)
+                epi.peer[r] = qp.ptrs[rank] if r == rank else send + (r - rank) * blk * es
+            with maybe(T, "gemm_qkv"):
+                lq.gemm(buf.h4, buf.h4sf, n, epi)
+            with maybe(T, "exchange"):
+                N.peer_push([(send + r * blk * es, qp.ptrs[r] + rank * blk * es, blk * es)
+                             for r in range(world) if r != rank])
+                self.sp.barrier(self.device)
             qa = buf.qkv_all.view(S, 3 * Hl * Dh)
+            q, k, v = qa[:, :Hl * Dh], qa[:, Hl * Dh:2 * Hl * Dh], qa[:, 2 * Hl * Dh:]
+            with maybe(T, "qknorm_rope"):
+                N.qknorm_rope(q, k, 3 * Hl * Dh, S, Hl, rot, b.q_norm, b.k_norm, rope_all, cfg.qk_eps)
             with maybe(T, "attention"):
-                self._attend(qa[:, :Hl * Dh], qa[:, Hl * Dh:2 * Hl * Dh], qa[:, 2 * Hl * Dh:], S, Hl, 3 * Hl * Dh,
-                             buf.o, ws)
-            with maybe(T, "all_to_all"):
-                self.sp.tokens_from_heads(buf.o, buf.o_recv)
+                m = self.attn_mask
+                if m is not None and m.S != S:
+                    raise ValueError(f"attn_mask is for S={m.S}, the sequence has S={S}")
+                N.attn_fp8_peers(q, k, v, 3 * Hl * Dh, Dh, S, Hl, op.ptrs, rank, Hl * Dh, ws,
+                                 kv_ptr=None if m is None else m.kv_ptr, kv_idx=None if m is None else m.kv_idx)
+            with maybe(T, "exchange"):
+                self.sp.barrier(self.device)
             src = dict(x=buf.o_recv, R=n, K=HD, ldx=Hl * Dh, cblk=Hl * Dh, blk_stride=n * Hl * Dh)
+        else:
+            with maybe(T, "gemm_qkv"):
+                lq.gemm(buf.h4, buf.h4sf, n, N.H3Epilogue(kind=N.H3_EPI_STORE, out=buf.qkv.data_ptr(), ldo=3 * HD))
+            rope = rope_all[t0:t0 + n]
+            q, k, v = buf.qkv[:, :HD], buf.qkv[:, HD:2 * HD], buf.qkv[:, 2 * HD:]
+            with maybe(T, "qknorm_rope"):
+                N.qknorm_rope(q, k, 3 * HD, n, H, rot, b.q_norm, b.k_norm, rope, cfg.qk_eps)
+            if self.sp is None:
+                with maybe(T, "attention"):
+                    self._attend(q, k, v, S, H, 3 * HD, buf.o, ws)
+                src = dict(x=buf.o, R=n, K=HD)
+            else:
+                Hl = H // world
+                with maybe(T, "all_to_all"):
+                    self.sp.qkv_heads_from_tokens(buf.qkv.view(n, 3, H, Dh), buf.qkv_all)
+                qa = buf.qkv_all.view(S, 3 * Hl * Dh)
+                with maybe(T, "attention"):
+                    self._attend(qa[:, :Hl * Dh], qa[:, Hl * Dh:2 * Hl * Dh], qa[:, 2 * Hl * Dh:], S, Hl,
+                                 3 * Hl * Dh, buf.o, ws)
+                with maybe(T, "all_to_all"):
+                    self.sp.tokens_from_heads(buf.o, buf.o_recv)
+                src = dict(x=buf.o_recv, R=n, K=HD, ldx=Hl * Dh, cblk=Hl * Dh, blk_stride=n * Hl * Dh)
         # ---- out-projection input -> NVFP4, out GEMM with the gated residual fused
         sl = self._slot(i, "out")
         with maybe(T, "quant_attn_out"):

@@ -16,7 +16,7 @@ import torch
 
 LIB_PATH = Path(os.environ.get("H3B200_LIB") or Path(__file__).resolve().parent / "_native" / "libh3b200.so")
 
-H3_EPI_STORE, H3_EPI_GATE_RESID, H3_EPI_ACT_BF16, H3_EPI_ACT_Q = 0, 1, 2, 3
+H3_EPI_STORE, H3_EPI_GATE_RESID, H3_EPI_ACT_BF16, H3_EPI_ACT_Q, H3_EPI_STORE_PEERS = 0, 1, 2, 3, 4
 ACT_GELU, ACT_SWIGLU = 0, 1
 SLOT_FLOATS = 4   # H3ScaleSlot: amax, act, used, margin
 
@@ -25,7 +25,12 @@ vp, i32, i64, f32, sz = C.c_void_p, C.c_int, C.c_longlong, C.c_float, C.c_size_t
 
 class H3Epilogue(C.Structure):
     _fields_ = [("kind", i32), ("out", vp), ("ldo", i64), ("x", vp), ("ldx", i64), ("mod", vp), ("idx", vp),
-                ("gate_part", i32), ("act_kind", i32), ("qcodes", vp), ("qsf", vp), ("q_slot", vp)]
+                ("gate_part", i32), ("act_kind", i32), ("qcodes", vp), ("qsf", vp), ("q_slot", vp),
+                ("peer", vp * 8), ("ranks", i32), ("rank", i32)]
+
+
+class H3PeerCopy(C.Structure):
+    _fields_ = [("src", vp), ("dst", vp), ("bytes", sz)]
 
 
 # name -> argtypes (restype int unless noted)
@@ -48,6 +53,12 @@ _SIGS = {
     "h3_attn_fp8": [vp, vp, vp, i64, i64, i32, i32, vp, i64, vp, sz, vp],
     "h3_attn_fp8_noalloc": [vp, vp, vp, i64, i64, i32, i32, vp, i64, vp],
     "h3_attn_fp8_sparse": [vp, vp, vp, i64, i64, i32, i32, vp, vp, vp, i64, vp, sz, vp],
+    "h3_attn_fp8_peers": [vp, vp, vp, i64, i64, i32, i32, vp, vp, C.POINTER(vp), i32, i32, i64, vp, sz, vp],
+    "h3_peer_alloc": [sz, C.POINTER(vp), vp],
+    "h3_peer_open": [vp, C.POINTER(vp)],
+    "h3_peer_close": [vp],
+    "h3_peer_free": [vp],
+    "h3_peer_push": [C.POINTER(H3PeerCopy), i32, vp],
 }
 
 _lib = None
@@ -205,3 +216,73 @@ def attn_fp8_sparse(q, k, v, ld, hstride, S, H, kv_ptr, kv_idx, out, ldo, worksp
     check(lib().h3_attn_fp8_sparse(ptr(q), ptr(k), ptr(v), ld, hstride, S, H, ptr(kv_ptr), ptr(kv_idx), ptr(out), ldo,
                                    ptr(workspace), workspace.numel() * workspace.element_size(), stream()),
           "h3_attn_fp8_sparse")
+
+
+def attn_fp8_peers(q, k, v, ld, hstride, S, H, peers: list[int], rank: int, ldo, workspace, kv_ptr=None,
+                   kv_idx=None) -> None:
+    """Attention of this rank's H heads over all S tokens, each output row stored to the receive buffer of the rank
+    that owns the token (``peers``: every rank's buffer as mapped here)."""
+
+    _count(4)
+    arr = (vp * len(peers))(*peers)
+    check(lib().h3_attn_fp8_peers(ptr(q), ptr(k), ptr(v), ld, hstride, S, H, ptr(kv_ptr), ptr(kv_idx), arr,
+                                  len(peers), rank, ldo, ptr(workspace), workspace.numel() * workspace.element_size(),
+                                  stream()), "h3_attn_fp8_peers")
+
+
+# ---- device buffers shared between the processes of one node (CUDA IPC), for the fused Ulysses exchanges
+IPC_HANDLE_BYTES = 64
+
+
+def peer_alloc(nbytes: int) -> tuple[int, bytes]:
+    """A device allocation of the current device and its IPC handle (free it with peer_free)."""
+
+    p = vp()
+    h = C.create_string_buffer(IPC_HANDLE_BYTES)
+    check(lib().h3_peer_alloc(nbytes, C.byref(p), h), "h3_peer_alloc")
+    return p.value, h.raw
+
+
+def peer_open(handle: bytes) -> int:
+    """Maps another process's peer_alloc buffer into this one (close it with peer_close)."""
+
+    if len(handle) != IPC_HANDLE_BYTES:
+        raise ValueError(f"an IPC handle has {IPC_HANDLE_BYTES} bytes, got {len(handle)}")
+    p = vp()
+    check(lib().h3_peer_open(C.create_string_buffer(handle, IPC_HANDLE_BYTES), C.byref(p)), "h3_peer_open")
+    return p.value
+
+
+def peer_push(copies: list[tuple[int, int, int]]) -> None:
+    """(src, dst, bytes) contiguous copies in one kernel on the current stream, e.g. into other ranks' buffers."""
+
+    _count(1)
+    arr = (H3PeerCopy * len(copies))(*[H3PeerCopy(s, d, b) for s, d, b in copies])
+    check(lib().h3_peer_push(arr, len(copies), stream()), "h3_peer_push")
+
+
+def peer_close(p: int) -> None:
+    check(lib().h3_peer_close(p), "h3_peer_close")
+
+
+def peer_free(p: int) -> None:
+    check(lib().h3_peer_free(p), "h3_peer_free")
+
+
+class _DeviceArray:
+    """__cuda_array_interface__ of a raw device allocation, so torch can view it without a copy."""
+
+    def __init__(self, p: int, shape: tuple[int, ...], typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (p, False), "version": 3,
+                                         "strides": None}
+
+
+_TYPESTR = {torch.bfloat16: "<i2", torch.int16: "<i2", torch.uint8: "|u1", torch.float32: "<f4"}
+
+
+def tensor_at(p: int, shape: tuple[int, ...], dtype: torch.dtype, device) -> torch.Tensor:
+    """A torch tensor over the device memory at p (no copy; the caller keeps the memory alive).  bf16 has no
+    array-interface type string: the 2-byte words are viewed as int16 and reinterpreted."""
+
+    t = torch.as_tensor(_DeviceArray(p, shape, _TYPESTR[dtype]), device=device)
+    return t.view(torch.bfloat16) if dtype == torch.bfloat16 else t

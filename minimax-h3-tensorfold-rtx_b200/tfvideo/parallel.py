@@ -5,12 +5,21 @@ gated residuals are token-local.  Around attention, one all-to-all per tensor tu
 [S, H/P, Dh] (every token, this rank's heads), and one more brings the output [S, H/P * Dh] back to
 [S/P, H * Dh] -- received as P column blocks [P, S/P, H/P * Dh], which the out-projection's quantiser reads in place.
 The reference runs on one GPU and has no collective; this is the B200 build's multi-GPU layer.
+
+On GPUs the engine does both exchanges inside the kernels that produce the data: the qkv GEMM's epilogue and the
+attention kernel's epilogue store each head's columns / each token's row straight into the owning rank's receive
+buffer (a PeerBuffer: device memory every rank maps through CUDA IPC), and a barrier after the kernel stands in for
+the all-to-all.  The all-to-all methods below remain for library attention backends and CPU (gloo) runs.
 """
 
 from __future__ import annotations
 
+import math
+
 import torch
 import torch.distributed as dist
+
+from . import native as N
 
 
 class SequenceParallel:
@@ -61,6 +70,28 @@ class SequenceParallel:
     def max_(self, t: torch.Tensor) -> torch.Tensor:
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
         return t
+
+    def barrier(self, device) -> None:
+        """In stream order: returns (on the device) once every rank's work before it has finished, so the peer stores
+        that work made are visible to what follows (a one-element all-reduce)."""
+
+        if getattr(self, "_flag", None) is None or self._flag.device != torch.device(device):
+            self._flag = torch.zeros(1, dtype=torch.float32, device=device)
+        dist.all_reduce(self._flag, group=self.group)
+
+
+class PeerBuffer:
+    """A device buffer this rank owns and every rank of the group stores into: a plain allocation shared through
+    CUDA IPC (no multicast object), mapped by each rank once.  ``ptrs[r]`` is rank r's buffer as mapped here;
+    ``tensor`` views this rank's own.  The mappings last until the process exits."""
+
+    def __init__(self, sp: SequenceParallel, shape: tuple[int, ...], dtype: torch.dtype, device):
+        nbytes = math.prod(shape) * torch.empty((), dtype=dtype).element_size()
+        local, handle = N.peer_alloc(nbytes)
+        handles = [None] * sp.world
+        dist.all_gather_object(handles, handle, group=sp.group)
+        self.ptrs = [local if r == sp.rank else N.peer_open(handles[r]) for r in range(sp.world)]
+        self.tensor = N.tensor_at(local, shape, dtype, device)
 
 
 def unshard_columns(recv: torch.Tensor) -> torch.Tensor:
