@@ -137,3 +137,38 @@ def test_shard_requires_even_split():
     assert sp.shard(37760) == (3 * 4720, 4720)
     with pytest.raises(ValueError):
         sp.shard(37790)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_peer_store_layout_matches_all_to_all(world):
+    """The GPU exchange's index arithmetic, restated element by element: the qkv GEMM's STORE_PEERS epilogue
+    (csrc/gemm_nvfp4.cuh) writes column (part, head, d) of local row `row` to base[owner] + ((rank * n + row) * 3 +
+    part) * Hr * 128 + (head % Hr) * 128 + d with the bases the engine passes (its own receive buffer for its own
+    heads, staging + (r - rank) * block for rank r's), and h3_peer_push then copies staging block r to rank r's
+    receive buffer at row rank * n.  The result must equal the all-to-all's [S, 3, H/P, Dh] receive layout."""
+
+    n, H, Dh = 3, 2 * world, 128
+    Hr, S = H // world, n * world
+    blk = n * 3 * Hr * Dh
+    g = torch.Generator().manual_seed(11)
+    local = [torch.randn(n, 3, H, Dh, generator=g) for _ in range(world)]
+    recv = [torch.full((S * 3 * Hr * Dh,), float("nan")) for _ in range(world)]
+    for rank in range(world):
+        stage = torch.full((world * blk,), float("nan"))
+        # bases: ("recv", q) = q's receive buffer; ("stage", off) = this rank's staging buffer at element offset off
+        base = [("recv", rank, 0) if r == rank else ("stage", rank, (r - rank) * blk) for r in range(world)]
+        for row in range(n):
+            for part in range(3):
+                for head in range(H):
+                    owner = head // Hr
+                    off = ((rank * n + row) * 3 + part) * Hr * 128 + (head - owner * Hr) * 128
+                    kind, _, b0 = base[owner]
+                    dst = recv[rank] if kind == "recv" else stage
+                    dst[b0 + off:b0 + off + Dh] = local[rank][row, part, head]
+        for r in range(world):   # the push
+            if r != rank:
+                recv[r][rank * blk:(rank + 1) * blk] = stage[r * blk:(r + 1) * blk]
+    full = torch.cat(local)   # [S, 3, H, Dh], tokens in rank order
+    for q in range(world):
+        want = full[:, :, q * Hr:(q + 1) * Hr, :].reshape(-1)
+        assert torch.equal(recv[q], want)
