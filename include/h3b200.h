@@ -138,6 +138,9 @@ typedef struct H3PeerCopy {
  * time, so writes to another GPU cross NVLink in full packets (row-scattered 16-byte stores do not).  Like any
  * kernel's, its writes are visible to work ordered after its completion (for another rank: after a barrier). */
 int h3_peer_push(const H3PeerCopy* copies, int n, void* stream);
+/* The same copies (any number) as cudaMemcpyAsync device-to-device calls on `stream`, one per copy: the copy engines
+ * move the data, so it overlaps kernels that hold every SM (a persistent GEMM). */
+int h3_peer_copy(const H3PeerCopy* copies, int n, void* stream);
 
 /* ---------------------------------------------------------------------------------------------- GEMM */
 /* NVFP4 W4A4 GEMM y = A x B^T (replaces Nvfp4Linear.__call__ -> TensorFold prompt(A4, x, lin),

@@ -269,6 +269,18 @@ int h3_peer_push(const H3PeerCopy* copies, int n, void* stream) {
   return check_launch("h3_peer_push");
 }
 
+int h3_peer_copy(const H3PeerCopy* copies, int n, void* stream) {
+  if (!copies || n < 0) return fail(H3_ERR_ARG, "h3_peer_copy: NULL copies or n < 0");
+  for (int c = 0; c < n; ++c) {
+    if (!copies[c].bytes) continue;
+    if (!copies[c].src || !copies[c].dst) return fail(H3_ERR_ARG, "h3_peer_copy: copy %d has a NULL pointer", c);
+    cudaError_t e = cudaMemcpyAsync(copies[c].dst, copies[c].src, copies[c].bytes, cudaMemcpyDeviceToDevice,
+                                    S_(stream));
+    if (e != cudaSuccess) return fail(H3_ERR_CUDA, "h3_peer_copy: copy %d: %s", c, cudaGetErrorString(e));
+  }
+  return H3_OK;
+}
+
 int h3_peer_free(void* ptr) {
   if (!ptr) return fail(H3_ERR_ARG, "h3_peer_free: NULL pointer");
   cudaError_t e = cudaFree(ptr);

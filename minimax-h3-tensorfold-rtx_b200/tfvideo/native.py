@@ -59,6 +59,7 @@ _SIGS = {
     "h3_peer_close": [vp],
     "h3_peer_free": [vp],
     "h3_peer_push": [C.POINTER(H3PeerCopy), i32, vp],
+    "h3_peer_copy": [C.POINTER(H3PeerCopy), i32, vp],
 }
 
 _lib = None
@@ -259,6 +260,15 @@ def peer_push(copies: list[tuple[int, int, int]]) -> None:
     _count(1)
     arr = (H3PeerCopy * len(copies))(*[H3PeerCopy(s, d, b) for s, d, b in copies])
     check(lib().h3_peer_push(arr, len(copies), stream()), "h3_peer_push")
+
+
+def peer_copy(copies: list[tuple[int, int, int]], stream_handle: int | None = None) -> None:
+    """(src, dst, bytes) copies by the copy engines (cudaMemcpyAsync), on torch's current stream unless given."""
+
+    if not copies:
+        return
+    arr = (H3PeerCopy * len(copies))(*[H3PeerCopy(s, d, b) for s, d, b in copies])
+    check(lib().h3_peer_copy(arr, len(copies), stream() if stream_handle is None else stream_handle), "h3_peer_copy")
 
 
 def peer_close(p: int) -> None:
