@@ -323,7 +323,11 @@ struct AttnArgs {
 constexpr int kQTile = 128;
 __host__ __device__ constexpr int attn_stages(int nt) { return nt == 2 ? 4 : 2; }    // K/V smem ring depth
 __host__ __device__ constexpr int attn_threads(int nt) { return 160 * nt + 32; }   // 5 warps a tile + TMA warp
-constexpr float kTau = 2.0f;        // running-max lag allowed before O is rescaled (log2 units)
+// Running-max lag allowed before O is rescaled (log2 units).  P of a row then stays within [2^-tau, 1] x 448 of
+// its max half by half, and O and l are rescaled only when a max grows by more than 2^tau.  6 against 2: block-sparse
+// 5.79 -> 5.47 ms at S = 37,760, H = 40 (its KV lists raise row maxima more often), dense unchanged; cosine against
+// fp32 SDPA unchanged to 1e-5 (0.99867 dense, 0.99863 sparse at S = 4096, H = 4).
+constexpr float kTau = 6.0f;
 constexpr float kPOffset = 8.807354922057604f - kTau;   // log2(448) - tau
 // Pairs of each 32-key chunk whose exp2 runs as a polynomial on the FMA pipe instead of the MUFU (bit i: keys 2i,
 // 2i + 1).  The MUFU completes 16 ex2 per cycle per SM, which alone would bound an FP8 tile's softmax at twice the
