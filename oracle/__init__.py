@@ -25,5 +25,7 @@ Pinning: ``tests/golden/make_golden.py`` runs the reference's own Triton kernels
 the build container and commits the outputs as fixtures; ``tests/test_oracle.py``
 checks this package against them.  TensorFold's activation quantiser and
 comfy-kitchen's RoPE are absent from the reference tree, so their exact bits are
-pinned only through the in-tree arithmetic they are called with.
+pinned only through the in-tree arithmetic they are called with: the quantiser of
+tfvideo/fp4attn.py:52-78 under the linear path's per-tensor scale, and the
+split-half RoPE convention stated in ops.py.
 """

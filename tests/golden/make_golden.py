@@ -28,9 +28,12 @@ HERE = Path(__file__).resolve().parent
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("H3_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("H3_REFERENCE"),
+                    help="checkout of the reference repository (or set H3_REFERENCE)")
     ap.add_argument("--out", default=str(HERE / "reference_kernels.npz"))
     a = ap.parse_args()
+    if not a.reference:
+        sys.exit("pass --reference (or H3_REFERENCE): the reference repository's checkout")
     if os.environ.get("TRITON_INTERPRET") != "1":
         sys.exit("set TRITON_INTERPRET=1 (the reference kernels run on the CPU interpreter)")
     sys.path.insert(0, a.reference)
