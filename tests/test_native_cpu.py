@@ -53,3 +53,41 @@ def test_calls_without_gpu_work_fail_cleanly(lib):
     assert "NULL" in native.last_error()
     assert lib.h3_sf_tiled_bytes(300, 5120) == 384 * 320
     assert lib.h3_attn_workspace_bytes(4096, 40) > 3 * 40 * 4096 * 128
+
+
+def test_peer_entry_points_check_their_arguments(lib):
+    """The multi-GPU entry points reject bad rank layouts and pointers on the host, before any CUDA call (the
+    pointers below are aligned placeholders that are never dereferenced)."""
+
+    from tfvideo import native as N
+
+    fake = 1 << 20   # 16-byte aligned, never touched
+    epi = N.H3Epilogue(kind=N.H3_EPI_STORE_PEERS, ranks=0, rank=0)
+    rc = lib.h3_gemm_nvfp4(fake, fake, fake, fake, fake, 1.0, None, 256, 3 * 128 * 4, 256, ctypes.byref(epi), None)
+    assert rc != 0 and "ranks" in N.last_error()
+    epi = N.H3Epilogue(kind=N.H3_EPI_STORE_PEERS, ranks=2, rank=2)
+    rc = lib.h3_gemm_nvfp4(fake, fake, fake, fake, fake, 1.0, None, 256, 3 * 128 * 4, 256, ctypes.byref(epi), None)
+    assert rc != 0 and "rank" in N.last_error()
+    epi = N.H3Epilogue(kind=N.H3_EPI_STORE_PEERS, ranks=4, rank=0)   # N = 3 * 128 * 2 does not split over 4
+    rc = lib.h3_gemm_nvfp4(fake, fake, fake, fake, fake, 1.0, None, 256, 3 * 128 * 2, 256, ctypes.byref(epi), None)
+    assert rc != 0 and "multiple" in N.last_error()
+    epi = N.H3Epilogue(kind=N.H3_EPI_STORE_PEERS, ranks=2, rank=1)
+    epi.peer[0] = fake
+    epi.peer[1] = fake + 8   # misaligned
+    rc = lib.h3_gemm_nvfp4(fake, fake, fake, fake, fake, 1.0, None, 256, 3 * 128 * 2, 256, ctypes.byref(epi), None)
+    assert rc != 0 and "peer[1]" in N.last_error()
+
+    peers = (ctypes.c_void_p * 2)(fake, fake)
+    rc = lib.h3_attn_fp8_peers(fake, fake, fake, 384, 128, 1000, 1, None, None, peers, 3, 0, 128, fake, 1 << 30, None)
+    assert rc != 0 and "ranks" in N.last_error()   # S = 1000 does not split over 3 ranks
+    rc = lib.h3_attn_fp8_peers(fake, fake, fake, 384, 128, 1024, 2, None, None, peers, 2, 0, 128, fake, 1 << 30, None)
+    assert rc != 0 and "H * 128" in N.last_error()   # receive rows shorter than this rank's heads
+    rc = lib.h3_attn_fp8_peers(fake, fake, fake, 384, 128, 1024, 1, fake, None, peers, 2, 0, 128, fake, 1 << 30, None)
+    assert rc != 0 and "tile list" in N.last_error()
+
+    copies = (N.H3PeerCopy * 1)(N.H3PeerCopy(fake, fake + 4, 64))
+    assert lib.h3_peer_push(copies, 1, None) != 0 and "aligned" in N.last_error()
+    assert lib.h3_peer_push(copies, 0, None) != 0 and "1..8" in N.last_error()
+    assert lib.h3_peer_copy(None, 1, None) != 0
+    assert lib.h3_peer_alloc(0, None, None) != 0 and "zero" in N.last_error()
+    assert lib.h3_peer_open(None, None) != 0
