@@ -27,6 +27,7 @@ from . import attention as A
 from . import kernels as K
 from . import linear as L
 from . import native as N
+from .parallel import QkvExchange
 from .profiling import maybe
 
 LIN_NAMES = ("qkv", "out", "fc1", "fc2")
@@ -332,35 +333,22 @@ class MiniMaxH3Engine:
             # (all S tokens, this rank's heads): the same per-(token, head) arithmetic as before the exchange.
             Hl, rank = H // world, self.sp.rank
             qp, op = buf.peers
-            C = 3 * Hl * Dh                           # elements of one token's row in a receive buffer
-            send, es = buf.qkv.data_ptr(), buf.qkv.element_size()
-
-            def bases(m0: int, M: int) -> list[int]:
-                # for a launch over local rows [m0, m0 + M), which adds (rank * M + row) rows to base r
-                shift = (rank * n + m0 - rank * M) * C * es
-                return [(qp.ptrs[rank] if r == rank else send + (r - rank) * n * C * es) + shift for r in range(world)]
-
-            def copies(r0: int, r1: int) -> list[tuple[int, int, int]]:
-                # rows [r0, r1) of every other rank's staged block -> that rank's receive buffer
-                return [(send + (r * n + r0) * C * es, qp.ptrs[r] + (rank * n + r0) * C * es, (r1 - r0) * C * es)
-                        for r in range(world) if r != rank]
-
+            xq = QkvExchange(rank, world, n, 3 * Hl * Dh, buf.qkv.element_size(), qp.ptrs, buf.qkv.data_ptr())
             # two row halves: the first half's blocks leave on the copy engines (no SMs) while the GEMM computes
             # the second; the second half's go by the push kernel once the GEMM has freed the SMs
-            m1 = (n // 2) // 128 * 128
-            parts = [(0, m1), (m1, n)] if m1 > 0 else [(0, n)]
+            parts = xq.row_parts()
             side = self.__dict__.setdefault("_side_stream", torch.cuda.Stream(device=self.device))
             with maybe(T, "gemm_qkv"):
                 for j, (r0, r1) in enumerate(parts):
                     epi = N.H3Epilogue(kind=N.H3_EPI_STORE_PEERS, ranks=world, rank=rank)
-                    for r, pp in enumerate(bases(r0, r1 - r0)):
+                    for r, pp in enumerate(xq.bases(r0, r1 - r0)):
                         epi.peer[r] = pp
                     lq.gemm(buf.h4[r0:r1], buf.h4sf[N.sf_tiled_bytes(r0, D) if r0 else 0:], r1 - r0, epi)
                     if j + 1 < len(parts):
                         side.wait_stream(torch.cuda.current_stream(self.device))
-                        N.peer_copy(copies(r0, r1), side.cuda_stream)
+                        N.peer_copy(xq.copies(r0, r1), side.cuda_stream)
             with maybe(T, "exchange"):
-                N.peer_push(copies(*parts[-1]))
+                N.peer_push(xq.copies(*parts[-1]))
                 torch.cuda.current_stream(self.device).wait_stream(side)
                 self.sp.barrier(self.device)
             qa = buf.qkv_all.view(S, 3 * Hl * Dh)

@@ -80,6 +80,43 @@ class SequenceParallel:
         dist.all_reduce(self._flag, group=self.group)
 
 
+class QkvExchange:
+    """Addresses of the fused qkv exchange of one rank (pure arithmetic, no device work).
+
+    The qkv GEMM's STORE_PEERS epilogue stores column (part, head, d) of its local row ``row`` to
+    ``base[owner] + ((rank * M + row) * 3 + part) * Hr * 128 + (head % Hr) * 128 + d`` (bf16 elements; M the launch's
+    rows, Hr = H / world).  This rank's own heads go straight into its receive buffer; every other rank's go into that
+    rank's contiguous block of a local staging buffer, [world, n, 3 Hr Dh], later copied to that rank's receive
+    buffer at row rank * n.  ``recv``: every rank's receive buffer as mapped here; ``send``: the staging buffer."""
+
+    def __init__(self, rank: int, world: int, n: int, row_elems: int, elem_bytes: int, recv: list[int], send: int):
+        self.rank, self.world, self.n = rank, world, n
+        self.row = row_elems * elem_bytes   # bytes of one token's row in a receive buffer (3 Hr Dh elements)
+        self.recv, self.send = recv, send
+
+    def row_parts(self, tile: int = 128) -> list[tuple[int, int]]:
+        """The GEMM's two row halves, split at a multiple of ``tile`` rows (one part when n is below two tiles)."""
+
+        m1 = (self.n // 2) // tile * tile
+        return [(0, m1), (m1, self.n)] if m1 > 0 else [(0, self.n)]
+
+    def bases(self, m0: int, M: int) -> list[int]:
+        """The epilogue's base for each rank, for a launch over local rows [m0, m0 + M) (the kernel adds
+        (rank * M + row) rows; the bases carry the rest of each destination's offset)."""
+
+        rank, n = self.rank, self.n
+        shift = (rank * n + m0 - rank * M) * self.row
+        return [(self.recv[rank] if r == rank else self.send + (r - rank) * n * self.row) + shift
+                for r in range(self.world)]
+
+    def copies(self, r0: int, r1: int) -> list[tuple[int, int, int]]:
+        """(src, dst, bytes): rows [r0, r1) of every other rank's staged block into that rank's receive buffer."""
+
+        rank, n = self.rank, self.n
+        return [(self.send + (r * n + r0) * self.row, self.recv[r] + (rank * n + r0) * self.row, (r1 - r0) * self.row)
+                for r in range(self.world) if r != rank]
+
+
 class PeerBuffer:
     """A device buffer this rank owns and every rank of the group stores into: a plain allocation shared through
     CUDA IPC (no multicast object), mapped by each rank once.  ``ptrs[r]`` is rank r's buffer as mapped here;

@@ -15,6 +15,7 @@ import traceback
 from datetime import timedelta
 from pathlib import Path
 
+import numpy as np
 import pytest
 import torch
 import torch.distributed as dist
@@ -140,35 +141,43 @@ def test_shard_requires_even_split():
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_peer_store_layout_matches_all_to_all(world):
-    """The GPU exchange's index arithmetic, restated element by element: the qkv GEMM's STORE_PEERS epilogue
-    (csrc/gemm_nvfp4.cuh) writes column (part, head, d) of local row `row` to base[owner] + ((rank * n + row) * 3 +
-    part) * Hr * 128 + (head % Hr) * 128 + d with the bases the engine passes (its own receive buffer for its own
-    heads, staging + (r - rank) * block for rank r's), and h3_peer_push then copies staging block r to rank r's
-    receive buffer at row rank * n.  The result must equal the all-to-all's [S, 3, H/P, Dh] receive layout."""
+@pytest.mark.parametrize("tile", [128, 2])   # 128: one GEMM launch at this n; 2: the two-row-half split
+def test_peer_store_layout_matches_all_to_all(world, tile):
+    """The fused qkv exchange's addresses (tfvideo.parallel.QkvExchange, as the engine uses them) with the qkv
+    GEMM's STORE_PEERS epilogue restated element by element (csrc/gemm_nvfp4.cuh: column (part, head, d) of launch
+    row `row` goes to base[owner] + ((rank * M + row) * 3 + part) * Hr * 128 + (head % Hr) * 128 + d), then the
+    block copies, on a simulated byte-addressed memory: every rank's receive buffer must end up in the all-to-all's
+    [S, 3, H/P, Dh] layout."""
 
-    n, H, Dh = 3, 2 * world, 128
+    sys.path.insert(0, str(ROOT / "minimax-h3-tensorfold-rtx_b200"))
+    from tfvideo.parallel import QkvExchange
+
+    n, H, Dh, es = 5, 2 * world, 128, 4          # fp32 elements stand in for bf16 (only the addresses matter)
     Hr, S = H // world, n * world
-    blk = n * 3 * Hr * Dh
-    g = torch.Generator().manual_seed(11)
-    local = [torch.randn(n, 3, H, Dh, generator=g) for _ in range(world)]
-    recv = [torch.full((S * 3 * Hr * Dh,), float("nan")) for _ in range(world)]
+    C = 3 * Hr * Dh
+    region = S * C * es                          # bytes of one receive buffer; staging buffers are as large
+    mem = np.full(2 * world * region // es, np.nan, dtype=np.float32)   # [recv of every rank | staging of every rank]
+    recv = [r * region for r in range(world)]
+    send = [world * region + r * region for r in range(world)]
+    g = np.random.RandomState(11)
+    local = [g.randn(n, 3, H, Dh).astype(np.float32) for _ in range(world)]
     for rank in range(world):
-        stage = torch.full((world * blk,), float("nan"))
-        # bases: ("recv", q) = q's receive buffer; ("stage", off) = this rank's staging buffer at element offset off
-        base = [("recv", rank, 0) if r == rank else ("stage", rank, (r - rank) * blk) for r in range(world)]
-        for row in range(n):
-            for part in range(3):
-                for head in range(H):
-                    owner = head // Hr
-                    off = ((rank * n + row) * 3 + part) * Hr * 128 + (head - owner * Hr) * 128
-                    kind, _, b0 = base[owner]
-                    dst = recv[rank] if kind == "recv" else stage
-                    dst[b0 + off:b0 + off + Dh] = local[rank][row, part, head]
-        for r in range(world):   # the push
-            if r != rank:
-                recv[r][rank * blk:(rank + 1) * blk] = stage[r * blk:(r + 1) * blk]
-    full = torch.cat(local)   # [S, 3, H, Dh], tokens in rank order
+        xq = QkvExchange(rank, world, n, C, es, recv, send[rank])
+        parts = xq.row_parts(tile)
+        assert parts[0][0] == 0 and parts[-1][1] == n and all(a[1] == b[0] for a, b in zip(parts, parts[1:]))
+        for r0, r1 in parts:
+            M, base = r1 - r0, xq.bases(r0, r1 - r0)
+            for row in range(M):
+                for part in range(3):
+                    for head in range(H):
+                        owner = head // Hr
+                        off = ((rank * M + row) * 3 + part) * Hr * 128 + (head - owner * Hr) * 128
+                        at = base[owner] // es + off
+                        mem[at:at + Dh] = local[rank][r0 + row, part, head]
+        for r0, r1 in parts:
+            for src, dst, nbytes in xq.copies(r0, r1):
+                mem[dst // es:(dst + nbytes) // es] = mem[src // es:(src + nbytes) // es]
+    full = np.concatenate(local)   # [S, 3, H, Dh], tokens in rank order
     for q in range(world):
-        want = full[:, :, q * Hr:(q + 1) * Hr, :].reshape(-1)
-        assert torch.equal(recv[q], want)
+        got = mem[recv[q] // es:(recv[q] + region) // es]
+        assert np.array_equal(got, full[:, :, q * Hr:(q + 1) * Hr, :].reshape(-1))
