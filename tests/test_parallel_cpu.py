@@ -130,6 +130,49 @@ def test_missing_rank_fails_collective():
     assert res[0].startswith("error"), res
 
 
+
+def _peer_buffer_worker(rank, world, port, q):
+    """PeerBuffer's rendezvous on gloo ranks, the CUDA IPC calls replaced by fakes that tag pointers and handles
+    with the owning rank: every rank must end up with its own allocation and every other rank's opened handle."""
+
+    try:
+        _init(rank, world, port)
+        from tfvideo import native as N
+        from tfvideo import parallel as P
+
+        opened = []
+        N.peer_alloc = lambda nbytes: (0x1000 * (rank + 1), bytes([rank]) * N.IPC_HANDLE_BYTES)
+        N.peer_open = lambda h: opened.append(h[0]) or 0x9000 + h[0]
+        N.tensor_at = lambda p, shape, dtype, device: torch.empty(shape, dtype=dtype)
+        sp = P.SequenceParallel()
+        pb = P.PeerBuffer(sp, (4, 3, 2, 8), torch.bfloat16, "cpu")
+        want = [0x1000 * (rank + 1) if r == rank else 0x9000 + r for r in range(world)]
+        assert pb.ptrs == want, (pb.ptrs, want)
+        assert sorted(opened) == [r for r in range(world) if r != rank]
+        assert tuple(pb.tensor.shape) == (4, 3, 2, 8) and pb.tensor.dtype == torch.bfloat16
+        sp.barrier("cpu")   # the barrier is a collective every rank passes
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception:  # noqa: BLE001
+        q.put((rank, traceback.format_exc()))
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_peer_buffer_rendezvous(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_peer_buffer_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in ps)
+    for p in ps:
+        p.join(30)
+        if p.is_alive():
+            p.kill()
+    assert all(v == "ok" for v in res.values()), res
+
+
 def test_shard_requires_even_split():
     from tfvideo.parallel import SequenceParallel
 
