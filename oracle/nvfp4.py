@@ -34,13 +34,18 @@ def f32(x) -> np.ndarray:
 def bf16_round(x) -> np.ndarray:
     """fp32 -> bf16 (round to nearest even) -> fp32, NaN kept quiet."""
 
+    # In 32-bit words: the largest non-NaN pattern is 0xFF800000 (-inf), and adding at most 0x8000 to it stays below
+    # 2^32, so the rounding carry never wraps; NaN patterns are replaced afterwards.
     x = f32(x)
-    b = x.view(np.uint32).astype(np.uint64)
+    if not x.flags.c_contiguous:
+        x = x.copy()
+    b = x.view(np.uint32)
+    r = ((b >> np.uint32(16)) & np.uint32(1)) + np.uint32(0x7FFF)
+    out = ((b + r) & np.uint32(0xFFFF0000)).view(np.float32)
     nan = np.isnan(x)
-    r = ((b >> 16) & 1) + 0x7FFF
-    b = ((b + r) >> 16) << 16
-    out = (b & 0xFFFFFFFF).astype(np.uint32).view(np.float32)
-    return np.where(nan, np.float32(np.nan), out).astype(np.float32)
+    if nan.any():
+        out = np.where(nan, np.float32(np.nan), out)
+    return out.astype(np.float32, copy=False)
 
 
 def bf16_trunc(x) -> np.ndarray:

@@ -209,13 +209,31 @@ def sdpa(q, k, v, tile_lists=None) -> np.ndarray:
     tile mask when ``tile_lists`` is given (rows with no kept key give zeros)."""
 
     q, k, v = (torch.from_numpy(f32(t)) for t in (q, k, v))
-    if tile_lists is None:
-        return torch.nn.functional.scaled_dot_product_attention(q, k, v).numpy()
-    keep = tile_key_mask(tile_lists, q.shape[1])
-    s = (q @ k.transpose(1, 2)) / math.sqrt(q.shape[2])
-    s = s.masked_fill(~keep, float("-inf"))
-    p = torch.softmax(s, -1).nan_to_num(0.0)
-    return (p @ v).numpy()
+    keep = None if tile_lists is None else tile_key_mask(tile_lists, q.shape[1])
+    return softmax_attention(q, k, v, keep).numpy()
+
+
+def softmax_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, keep: torch.Tensor | None = None,
+                      rows: int = 2048) -> torch.Tensor:
+    """softmax(q k^T / sqrt(Dh)) v in fp32, [H, Sq, Dh] x [H, Sk, Dh] -> [H, Sq, Dh], one head and ``rows`` query
+    rows at a time (explicit matmul -> softmax -> matmul: what SDPA's math backend computes; torch's fused CPU kernel
+    runs far slower than these matmuls on some hosts).  ``keep`` [Sq, Sk] masks keys; a row with no kept key gives
+    zeros."""
+
+    H, Sq, Dh = q.shape
+    out = torch.empty(H, Sq, v.shape[2], dtype=torch.float32)
+    scale = 1.0 / math.sqrt(Dh)
+    for h in range(H):
+        kh, vh = k[h].float(), v[h].float()
+        for r0 in range(0, Sq, rows):
+            s = (q[h, r0:r0 + rows].float() @ kh.T) * scale
+            if keep is not None:
+                s = s.masked_fill(~keep[r0:r0 + rows], float("-inf"))
+            p = torch.softmax(s, -1)
+            if keep is not None:
+                p = p.nan_to_num(0.0)
+            out[h, r0:r0 + rows] = p @ vh
+    return out
 
 
 def _e4m3(t: torch.Tensor) -> torch.Tensor:

@@ -166,3 +166,44 @@ def test_delayed_scale_policy():
     assert clipped == 1
     assert list(m) == [4.0, 4.0, 16.0]
     assert np.allclose(nxt, [10 / 2688 * 4, 10 / 2688 * 4, 1e-6 / 2688 * 16])
+
+
+# ------------------------------------------------------------------------------------------------ torch CPU path
+def test_torch_path_fake_quant_equals_oracle_quantiser():
+    """The torch restatement the CPU baseline times dequantises to exactly the oracle quantiser's values."""
+
+    import torch
+
+    from oracle import torch_path as TP
+
+    rs = np.random.RandomState(3)
+    x = N.bf16_round(rs.randn(96, 512).astype(np.float32) * np.where(rs.rand(512) < 0.02, 20.0, 1.0))
+    x[5, :16] = 0.0                                       # an all-zero group
+    got = TP.fake_quant(torch.from_numpy(x)).numpy()
+    g = N.global_scale(float(np.abs(x).max()))
+    ref = N.dequantize(*N.quantize(x, g), g)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def test_torch_path_block_matches_oracle_block():
+    """The timed CPU block computes the oracle's NVFP4 + SDPA block (same weights, inputs): cosine >= 0.999."""
+
+    import torch
+
+    from oracle import block as OB
+    from oracle import torch_path as TP
+
+    shape = OB.BlockShape(dim=256, heads=2, head_dim=128, ffn=512, act="gelu", rot_dim=128)
+    p = OB.make_params(shape, t_dim=8, seed=4)
+    S = 96
+    x = N.bf16_round(np.random.RandomState(5).randn(S, shape.dim).astype(np.float32))
+    t_emb = np.random.RandomState(6).randn(1, 8).astype(np.float32)
+    segs = [(0, S, 0)]
+    rope = OB.rope_table(S, 128)
+    ref = OB.block_forward(shape, p, x, t_emb, segs, rope, linears="nvfp4", attn="sdpa")
+    mod = torch.from_numpy(O.modulation(t_emb, p.ada_w, p.ada_b, shape.dim))
+    W = {n: torch.from_numpy(N.dequantize(*p.quantized()[n])) for n in ("qkv", "out", "fc1", "fc2")}
+    norms = {n: torch.from_numpy(getattr(p, n)) for n in ("norm1", "norm2", "q_norm", "k_norm")}
+    got = TP.block(torch.from_numpy(x), W, norms, mod, torch.zeros(S, dtype=torch.long), torch.from_numpy(rope),
+                   shape.heads).numpy()
+    assert O.cosine(got - x, ref - x) >= 0.999
