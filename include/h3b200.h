@@ -81,6 +81,10 @@ int h3_last_error(char* buf, int n);
 /* Reads the device status word of the current device (0 = ok; else the code of the wait that gave up) and clears it
  * when reset != 0.  Synchronous. */
 int h3_device_status(int* status, int reset);
+/* In stream order, *dst = max(*dst, status word of the current device): a collective (max) over this value after a
+ * kernel lets every rank learn, on the device and without a host read, that some rank's bounded wait gave up.  No
+ * counterpart in the reference (one GPU). */
+int h3_status_publish(float* dst, void* stream);
 /* Bytes of a tiled NVFP4 scale buffer for `rows` x `cols` elements: ceil(rows / 128) * 128 * cols / 16.  The GEMM
  * reads A and B scales in this layout (512-byte atoms of 128 rows x 4 groups: byte
  * (r % 32) * 16 + (r / 32 % 4) * 4 + g % 4 of atom [r / 128][g / 4]). */
@@ -195,9 +199,10 @@ int h3_attn_fp8_peers(const void* q, const void* k, const void* v, long long ld,
  * array inside this library, held by every GPU that loads the library until the process exits; problems whose
  * h3_attn_workspace_bytes(S, H) exceed 64 MiB - 1 KiB (about S * H <= 170,000, e.g. S = 4096 at H = 40) are
  * rejected with H3_ERR_SHAPE.  The first call on a device looks up the array's device address (make it before any
- * stream capture).  All calls share the array, so calls that overlap on the GPU (other streams, other threads) race;
- * nothing in it needs to start at zero.  It allocates nothing.  This entry point has no counterpart in the
- * reference. */
+ * stream capture); the address is kept per CUDA context, so a call made in another context on that device, or after
+ * a device reset, looks it up again for that context.  All calls share the array, so calls that overlap on the GPU
+ * (other streams, other threads) race; nothing in it needs to start at zero.  It allocates nothing.  This entry point
+ * has no counterpart in the reference. */
 int h3_attn_fp8_noalloc(const void* q, const void* k, const void* v, long long ld, long long hstride, int S, int H,
                         void* out, long long ldo, void* stream);
 

@@ -185,6 +185,20 @@ int h3_device_status(int* status, int reset) {
   return H3_OK;
 }
 
+}  // extern "C"
+
+namespace {
+__global__ void status_publish_kernel(float* dst) { *dst = fmaxf(*dst, (float)*(volatile int*)&g_status); }
+}  // namespace
+
+extern "C" {
+
+int h3_status_publish(float* dst, void* stream) {
+  if (!dst || !aligned(dst, 4)) return fail(H3_ERR_ARG, "h3_status_publish: dst NULL or misaligned");
+  status_publish_kernel<<<1, 1, 0, S_(stream)>>>(dst);
+  return check_launch("h3_status_publish");
+}
+
 size_t h3_sf_tiled_bytes(int rows, int cols) {
   if (rows <= 0 || cols <= 0) return 0;
   return (size_t)((rows + 127) / 128) * 128 * (size_t)(cols / 16);
@@ -584,23 +598,54 @@ constexpr size_t kNoAllocScratchBytes = 64ull << 20;
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
 namespace {
-std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[64] = {};
+// The array's device address is looked up once per (device, CUDA context) and cached with the context it belongs to:
+// a caller that resets the device or switches to another context on it gets the module loaded again, possibly at a
+// different address, and the lookup is then repeated for that context.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
 
-int noalloc_scratch(void** out) {
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
+
+struct NoAllocSlot {
+  CUcontext ctx;
+  void* ptr;
+};
+std::mutex g_noalloc_mu;
+NoAllocSlot g_noalloc[64] = {};
+
+int noalloc_scratch(const char* who, void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return fail(H3_ERR_CUDA, "h3_attn_fp8_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= 64) return fail(H3_ERR_ARG, "h3_attn_fp8_noalloc: device %d out of range", dev);
+  if (e != cudaSuccess) return fail(H3_ERR_CUDA, "%s: cudaGetDevice: %s", who, cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(H3_ERR_ARG, "%s: device %d out of range", who, dev);
+  CtxGetCurrentFn get = ctx_get_current_fn();
+  if (!get) return fail(H3_ERR_CUDA, "%s: cuCtxGetCurrent unavailable from the driver", who);
+  CUcontext ctx = nullptr;
+  if (get(&ctx) != CUDA_SUCCESS) return fail(H3_ERR_CUDA, "%s: cuCtxGetCurrent failed", who);
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || !p)
-      return fail(H3_ERR_CUDA, "h3_attn_fp8_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    g_noalloc_ptr[dev] = p;
+  NoAllocSlot& slot = g_noalloc[dev];
+  if (ctx && slot.ptr && slot.ctx == ctx) {
+    *out = slot.ptr;
+    return H3_OK;
   }
-  *out = g_noalloc_ptr[dev];
+  // first call in this context (or none current yet: the runtime's lookup makes the device's primary context current)
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || !p) return fail(H3_ERR_CUDA, "%s: cudaGetSymbolAddress: %s", who, cudaGetErrorString(e));
+  if (get(&ctx) != CUDA_SUCCESS || !ctx) return fail(H3_ERR_CUDA, "%s: no current CUDA context after set-up", who);
+  slot.ctx = ctx;
+  slot.ptr = p;
+  *out = p;
   return H3_OK;
 }
 }  // namespace
@@ -609,19 +654,21 @@ extern "C" {
 
 int h3_attn_fp8_noalloc(const void* q, const void* k, const void* v, long long ld, long long hstride, int S, int H,
                         void* out, long long ldo, void* stream) {
-  if (S <= 0 || H <= 0) return fail(H3_ERR_SHAPE, "h3_attn_fp8_noalloc: S and H must be positive");
+  const char* who = "h3_attn_fp8_noalloc";
+  if (S <= 0 || H <= 0) return fail(H3_ERR_SHAPE, "%s: S and H must be positive", who);
   const size_t need = h3_attn_workspace_bytes(S, H);
   if (need + 1024 > kNoAllocScratchBytes)
     return fail(H3_ERR_SHAPE,
-                "h3_attn_fp8_noalloc: S=%d, H=%d needs %zu bytes of scratch, beyond the fixed %zu-byte array; use "
-                "h3_attn_fp8 with a caller-provided workspace",
-                S, H, need, kNoAllocScratchBytes - 1024);
+                "%s: S=%d, H=%d needs %zu bytes of scratch, beyond the fixed %zu-byte array; use h3_attn_fp8 with a "
+                "caller-provided workspace",
+                who, S, H, need, kNoAllocScratchBytes - 1024);
   void* base = nullptr;
-  int rc = noalloc_scratch(&base);
+  int rc = noalloc_scratch(who, &base);
   if (rc) return rc;
   // the workspace layout wants a 1024-byte aligned start; the array is 256-aligned, so step to the next 1024
   uint8_t* ws = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(base) + 1023) & ~uintptr_t(1023));
-  return h3_attn_fp8(q, k, v, ld, hstride, S, H, out, ldo, ws, kNoAllocScratchBytes - 1024, stream);
+  return attn_run(who, q, k, v, ld, hstride, S, H, nullptr, nullptr, out, ldo, ws, kNoAllocScratchBytes - 1024,
+                  stream);
 }
 
 }  // extern "C"

@@ -1,244 +1,340 @@
-"""ComfyUI's "TensorFold MiniMax H3 Loader" node on B200 (the reference's tfvideo/comfy_nodes.py:1-273).
+"""The ComfyUI loader node on B200: "TensorFold MiniMax H3 Loader" (reference: tfvideo/comfy_nodes.py).
 
-The node loads a MiniMax H3 DiT checkpoint into a B200 engine (converted to NVFP4 once, cached) and returns ComfyUI's
-own MiniMaxH3 MODEL built without blocks, whose ``blocks`` list is the engine's EngineBlocks: model sampling,
-sequence packing, conditioning, RoPE tables, the output heads and the VAE latents stay ComfyUI's, so a workflow
-swaps one loader node and keeps everything else.  The same node name, display name, inputs and defaults as the
-reference, so saved workflows load unchanged.
+What stays ComfyUI's: model sampling, sequence packing, conditioning, RoPE tables, the output heads and the VAE
+latents -- its own MiniMaxH3 model object, built here from the checkpoint's non-block tensors.  What the engine takes
+over: the 50 DiT blocks, whose slots in that model hold ``EngineBlock`` modules.  A workflow therefore swaps the loader
+node and nothing else.  The node keeps the reference's class name, display name, inputs, choice lists and defaults
+(comfy_nodes.py:242-273), because saved workflows refer to them.
 
-B200 differences:
-  * precision: "nvfp4" is this build's path.  The reference's "int8", "fp8", "nvfp4:edge=2" and "bf16-check" are
-    kept in the list (saved workflows carry them) and raise ValueError when chosen.
-  * attention: "auto" / "fp8" (libh3b200's FP8 kernel), "sdpa" / "cudnn" (PyTorch's); "fp4" and "int8" raise.
-  * every block stays resident in HBM, so there is no per-sequence memory plan and no block streaming; at the end of
-    a sampling run (ComfyUI's ON_CLEANUP) the activation buffers are released and the scales reset.
-LoRAs go through ComfyUI's LoRA nodes as in the reference: for an engine MODEL, ``load_lora_for_models`` hands the
-block-linear patches to the engine (merged into the source weights with ComfyUI's ``calculate_weight`` and
-re-quantised, cached per LoRA set) and everything else to ComfyUI's patcher.
+Pieces, each usable on its own:
+  ``EngineCache``   one resident engine per process, keyed by (checkpoint path, precision); NVFP4 conversion happens
+                    once and is cached on disk (tfvideo/store.py).
+  ``LoraBridge``    wraps ``comfy.sd.load_lora_for_models``: for a MODEL whose blocks are engine blocks, the LoRA
+                    patches that target block linears travel in the MODEL's transformer_options as a LoRA set, and
+                    every other patch goes to ComfyUI's patcher; at the first block of a forward the engine compares
+                    the set with its weights and, when it changed, re-converts with ComfyUI's ``calculate_weight``
+                    applied (cached per set).
+  ``ModelShell``    ComfyUI's MiniMaxH3 model without blocks, plus the engine's blocks, wrapped in a ModelPatcher with
+                    two hooks: a diffusion-model wrapper that rejects scheduled (hook) weight patches, which merged
+                    weights cannot follow, and an ON_CLEANUP callback that releases activations and resets the
+                    activation scales when a sampling run ends.
+B200 choices: precision "nvfp4" runs; the reference's other precisions stay in the list and are refused with
+ValueError.  Attention "auto" / "fp8" run libh3b200's FP8 kernel, "sdpa" / "cudnn" PyTorch's; "fp4" and "int8" are
+refused.  All blocks stay resident in HBM, so there is no memory plan and no block streaming.
 
-ComfyUI modules are imported inside the functions that need them; importing this module needs only torch.
+ComfyUI's modules are imported where they are used: importing this module needs only torch.
 """
 
 from __future__ import annotations
 
 import hashlib
 import logging
+from dataclasses import dataclass, field
 
 import torch
 
+log = logging.getLogger("tfvideo")
+
+# ---- node identity: fixed by the reference, saved workflows depend on it
 PRECISIONS = ["nvfp4", "int8", "nvfp4:edge=2", "fp8", "bf16-check"]
 ATTENTION = ["auto", "fp4", "fp8", "int8", "sdpa", "cudnn"]
-SUPPORTED_PRECISIONS = ("nvfp4",)
-LORA_KEY = "tfvideo_loras"          # transformer_options: [(fingerprint, {block key: adapter}, strength), ...]
-_ENGINE: dict = {}                  # the one resident engine: {"key": (path, spec), "engine": MiniMaxH3Engine}
+RUNNABLE_PRECISIONS = ("nvfp4",)
 
 
 def check_choices(precision: str, attention: str) -> str:
-    """The engine spec for a node's (precision, attention), or ValueError naming what this build cannot run."""
+    """Validate a node's (precision, attention) for this build; returns the conversion spec."""
 
     if precision not in PRECISIONS:
-        raise ValueError(f"precision {precision!r}: one of {PRECISIONS}")
-    if precision not in SUPPORTED_PRECISIONS:
-        raise ValueError(f"precision {precision!r} has no B200 build; use 'nvfp4'")
+        raise ValueError(f"unknown precision {precision!r} (choices: {', '.join(PRECISIONS)})")
+    if precision not in RUNNABLE_PRECISIONS:
+        raise ValueError(f"precision {precision!r} is not built for B200: choose 'nvfp4'")
     from . import attention as A
 
-    A.get(attention)                # raises ValueError for "fp4" / "int8" / unknown names
+    A.get(attention)                               # ValueError for 'fp4', 'int8' and unknown backends
     return precision
 
 
-def _engine(path: str, spec: str):
-    from . import store
+# ------------------------------------------------------------------------------------------------ engine cache
+class EngineCache:
+    """The process's one resident engine.  Asking for another (path, spec) drops the current engine first, so two
+    sets of block weights never share the GPU."""
 
-    if _ENGINE.get("key") == (path, spec):
-        return _ENGINE["engine"]
-    _ENGINE.clear()
-    torch.cuda.empty_cache()
-    engine = store.load_or_convert(path, spec, device="cuda", log=logging.info)
-    engine.on_forward = _on_forward
-    _ENGINE.update(key=(path, spec), engine=engine)
-    return engine
+    def __init__(self):
+        self.ident: tuple[str, str] | None = None
+        self.engine = None
+
+    def acquire(self, path: str, spec: str, on_forward=None):
+        if self.ident == (path, spec) and self.engine is not None:
+            return self.engine
+        self.ident, self.engine = None, None
+        torch.cuda.empty_cache()
+        from . import store
+
+        engine = store.load_or_convert(path, spec, device="cuda", log=log.info)
+        engine.on_forward = on_forward
+        self.ident, self.engine = (path, spec), engine
+        return engine
 
 
 # ------------------------------------------------------------------------------------------------ LoRA
-def fingerprint(part: dict) -> str:
-    """A short signature of a LoRA's block-linear patches: their keys, shapes and first values."""
+@dataclass
+class LoraEntry:
+    """One LoRA applied to an engine MODEL: its block-linear adapters (model key -> ComfyUI adapter) and strength."""
 
-    h = hashlib.sha1()
-    for k in sorted(part):
-        h.update(k.encode())
-        for t in getattr(part[k], "weights", ()):
-            if torch.is_tensor(t):
-                h.update(str(tuple(t.shape)).encode())
-                h.update(t.flatten()[:64].float().cpu().numpy().tobytes())
-    return h.hexdigest()[:16]
+    adapters: dict
+    strength: float
+    digest: str = field(default="")
 
-
-def lora_signature(loras) -> str:
-    return "|".join(f"{fp}x{strength:.4f}" for fp, _, strength in loras)
+    def __post_init__(self):
+        if not self.digest:
+            self.digest = LoraBridge.digest(self.adapters)
 
 
-def lora_patches(loras) -> dict[str, list]:
-    """{block linear name (e.g. ``blocks.3.mlp.fc1``): ComfyUI patch list} from the transformer_options LoRA set."""
+class LoraBridge:
+    """Routes LoRA weight patches between the engine (block linears) and ComfyUI's patcher (everything else)."""
 
-    patches: dict[str, list] = {}
-    for _, part, strength in loras:
-        for key, adapter in part.items():
-            name = key[len("diffusion_model."):-len(".weight")]
-            patches.setdefault(name, []).append((strength, adapter, 1.0, None, None))
-    return patches
+    OPTION = "tfvideo_loras"          # transformer_options key holding the MODEL's list of LoraEntry
 
+    # -- naming
+    @staticmethod
+    def block_aliases(layers: int) -> dict[str, str]:
+        """Every name a LoRA file may use for a block linear -> its model key ``diffusion_model.blocks.i.<lin>.weight``
+        (ComfyUI's dotted key without ``.weight``, and the kohya-style ``lora_unet_blocks_i_<lin>``)."""
 
-def _on_forward(engine, S, transformer_options):
-    """Block 0 of each forward: bring the engine's weights in line with the MODEL's LoRA set."""
+        from .minimax_h3 import SOURCE
 
-    _sync_loras(engine, transformer_options)
+        out = {}
+        for i in range(layers):
+            for lin in SOURCE.values():
+                model_key = f"diffusion_model.blocks.{i}.{lin}.weight"
+                out[model_key.removesuffix(".weight")] = model_key
+                out[f"lora_unet_blocks_{i}_{lin.replace('.', '_')}"] = model_key
+        return out
 
+    @staticmethod
+    def linear_name(model_key: str) -> str:
+        """``diffusion_model.blocks.3.mlp.fc1.weight`` -> ``blocks.3.mlp.fc1`` (the engine's name for the linear)."""
 
-def _sync_loras(engine, transformer_options):
-    loras = (transformer_options or {}).get(LORA_KEY, [])
-    sig = lora_signature(loras)
-    if sig == engine.lora_sig:
-        return
-    import comfy.lora
+        return model_key.removeprefix("diffusion_model.").removesuffix(".weight")
 
-    from . import store
+    # -- identity of a LoRA set
+    @staticmethod
+    def digest(adapters: dict) -> str:
+        """A short content digest of a LoRA's block adapters: keys, tensor shapes and leading values."""
 
-    patches = lora_patches(loras)
+        h = hashlib.blake2b(digest_size=8)
+        for k in sorted(adapters):
+            h.update(k.encode())
+            for t in getattr(adapters[k], "weights", ()):
+                if torch.is_tensor(t):
+                    h.update(repr(tuple(t.shape)).encode())
+                    h.update(t.detach().reshape(-1)[:64].float().cpu().numpy().tobytes())
+        return h.hexdigest()
 
-    def merge(name, w):
-        p = patches.get(name)
-        return comfy.lora.calculate_weight(p, w, name) if p else None
+    @staticmethod
+    def signature(entries) -> str:
+        """The cache identity of an ordered LoRA set ("" for none)."""
 
-    logging.info(f"[tfvideo] LoRA set changed ({len(loras)} LoRA(s)): "
-                 f"{'re-merging' if loras else 'restoring base weights'}")
-    engine.release_vram()
-    new = store.load_or_convert(engine.source, engine.kind, device="cuda", log=logging.info,
-                                merge=merge if loras else None, merge_sig=sig)
-    engine.replace_blocks(new.blocks, sig, slots=new.slots)
+        return ";".join(f"{e.digest}@{e.strength:.4f}" for e in entries)
 
+    @staticmethod
+    def patch_lists(entries) -> dict[str, list]:
+        """Engine linear name -> the patch list ComfyUI's ``calculate_weight`` takes, in application order."""
 
-def block_key_map(layers: int) -> dict[str, str]:
-    """ComfyUI LoRA key aliases of the block linears -> their model keys (``diffusion_model.blocks.i.<lin>.weight``)."""
+        lists: dict[str, list] = {}
+        for e in entries:
+            for model_key, adapter in e.adapters.items():
+                lists.setdefault(LoraBridge.linear_name(model_key), []).append((e.strength, adapter, 1.0, None, None))
+        return lists
 
-    from .minimax_h3 import SOURCE
+    # -- ComfyUI side
+    @staticmethod
+    def engine_of(model):
+        """The engine behind a ComfyUI MODEL, or None for any other model."""
 
-    key_map = {}
-    for i in range(layers):
-        for src in SOURCE.values():
-            k = f"diffusion_model.blocks.{i}.{src}.weight"
-            key_map[k[:-len(".weight")]] = k
-            key_map["lora_unet_blocks_{}_{}".format(i, src.replace(".", "_"))] = k
-    return key_map
+        inner = getattr(getattr(model, "model", None), "diffusion_model", None)
+        return getattr(inner, "tfvideo_engine", None)
 
+    @classmethod
+    def install(cls) -> None:
+        """Wrap ``comfy.sd.load_lora_for_models`` once per process."""
 
-def _install_lora_hook():
-    import comfy.sd
+        import comfy.sd
 
-    original = comfy.sd.load_lora_for_models
-    if getattr(original, "_tfvideo", False):
-        return
+        stock = comfy.sd.load_lora_for_models
+        if getattr(stock, "tfvideo_bridge", False):
+            return
 
-    def load_lora_for_models(model, clip, lora, strength_model, strength_clip, lora_metadata=None):
-        engine = getattr(getattr(getattr(model, "model", None), "diffusion_model", None), "tfvideo_engine", None)
-        if engine is None or strength_model == 0:
-            return original(model, clip, lora, strength_model, strength_clip, lora_metadata)
+        def load_lora_for_models(model, clip, lora, strength_model, strength_clip, lora_metadata=None):
+            engine = cls.engine_of(model)
+            if engine is None or strength_model == 0:
+                return stock(model, clip, lora, strength_model, strength_clip, lora_metadata)
+            new_model = cls.split_into(model, engine, lora, float(strength_model), lora_metadata)
+            new_clip = None
+            if clip is not None:                      # the text encoder's part: ComfyUI's own path, model strength 0
+                new_clip = stock(None, clip, lora, 0.0, strength_clip, lora_metadata)[1]
+            return new_model, new_clip
+
+        load_lora_for_models.tfvideo_bridge = True
+        comfy.sd.load_lora_for_models = load_lora_for_models
+
+    @classmethod
+    def split_into(cls, model, engine, lora: dict, strength: float, lora_metadata=None):
+        """A clone of ``model`` carrying the LoRA: block-linear adapters appended to its LoRA set, the rest patched
+        by ComfyUI."""
+
         import comfy.lora
         import comfy.lora_convert
 
-        key_map = comfy.lora.model_lora_keys_unet(model.model, {})
-        blocks = block_key_map(len(engine.blocks))
-        key_map.update(blocks)
-        block_keys = set(blocks.values())
-        loaded = comfy.lora.load_lora(comfy.lora_convert.convert_lora(lora), key_map)
-        part = {k: v for k, v in loaded.items() if k in block_keys}
-        rest = {k: v for k, v in loaded.items() if k not in block_keys}
-        new_model = model.clone()
-        new_model.add_patches(rest, strength_model)
-        to = dict(new_model.model_options.get("transformer_options", {}))
-        to[LORA_KEY] = list(to.get(LORA_KEY, [])) + [(fingerprint(part), part, float(strength_model))]
-        new_model.model_options["transformer_options"] = to
+        aliases = cls.block_aliases(len(engine.blocks))
+        keys = comfy.lora.model_lora_keys_unet(model.model, {})
+        keys.update(aliases)
+        loaded = comfy.lora.load_lora(comfy.lora_convert.convert_lora(lora), keys)
+        engine_keys = set(aliases.values())
+        blocks = {k: a for k, a in loaded.items() if k in engine_keys}
+        others = {k: a for k, a in loaded.items() if k not in engine_keys}
+        clone = model.clone()
+        clone.add_patches(others, strength)
+        options = dict(clone.model_options.get("transformer_options", {}))
+        options[cls.OPTION] = [*options.get(cls.OPTION, []), LoraEntry(blocks, strength)]
+        clone.model_options["transformer_options"] = options
         if lora_metadata:
-            new_model.set_attachments("lora_metadata", lora_metadata)
-        logging.info(f"[tfvideo] LoRA: {len(part)} block linears to the engine, {len(rest)} other weights to ComfyUI")
-        new_clip = None
-        if clip is not None:
-            _, new_clip = original(None, clip, lora, 0.0, strength_clip, lora_metadata)
-        return new_model, new_clip
+            clone.set_attachments("lora_metadata", lora_metadata)
+        log.info("[tfvideo] LoRA at strength %.3f: %d block linear(s) merged by the engine, %d tensor(s) patched "
+                 "by ComfyUI", strength, len(blocks), len(others))
+        return clone
 
-    load_lora_for_models._tfvideo = True
-    comfy.sd.load_lora_for_models = load_lora_for_models
+    # -- engine side (called at block 0 of every forward)
+    @classmethod
+    def sync(cls, engine, transformer_options) -> bool:
+        """Bring the engine's weights to the MODEL's LoRA set; True when it re-converted."""
+
+        entries = list((transformer_options or {}).get(cls.OPTION, []))
+        sig = cls.signature(entries)
+        if sig == engine.lora_sig:
+            return False
+        from . import store
+
+        merge = None
+        if entries:
+            import comfy.lora
+
+            lists = cls.patch_lists(entries)
+
+            def merge(name, w):
+                return comfy.lora.calculate_weight(lists[name], w, name) if name in lists else None
+        log.info("[tfvideo] engine weights follow a new LoRA set (%d LoRA(s))%s", len(entries),
+                 "" if entries else ": back to the base checkpoint")
+        engine.release_vram()
+        fresh = store.load_or_convert(engine.source, engine.kind, device="cuda", log=log.info, merge=merge,
+                                      merge_sig=sig)
+        engine.replace_blocks(fresh.blocks, sig, slots=fresh.slots)
+        return True
+
+
+def on_forward(engine, S, transformer_options) -> None:
+    """The engine's per-forward hook (block 0): keep its weights in line with the MODEL's LoRA set."""
+
+    LoraBridge.sync(engine, transformer_options)
 
 
 # ------------------------------------------------------------------------------------------------ the MODEL
-def build_model(path: str, engine):
-    """ComfyUI's MiniMaxH3 MODEL from the checkpoint's non-block tensors, with the engine's blocks."""
+class ModelShell:
+    """ComfyUI's MiniMaxH3 model for a checkpoint, built without its DiT blocks, then given the engine's."""
 
-    import comfy.model_detection
-    import comfy.model_management as mm
-    import comfy.model_patcher
-    import comfy.patcher_extension
+    def __init__(self, path: str):
+        from .source import SafeTensors
 
-    from .minimax_h3 import EngineBlock
-    from .source import SafeTensors
+        self.path = path
+        self.file = SafeTensors(path)
 
-    f = SafeTensors(path)
-    probe = {k: torch.empty(f.shape(k), device="meta") for k in f.keys()}
-    prefix = comfy.model_detection.unet_prefix_from_state_dict(probe)
-    if not any(k.startswith(prefix) for k in probe):
-        prefix = ""
-    unet_config = comfy.model_detection.detect_unet_config(probe, prefix)
-    if unet_config is None or unet_config.get("image_model") != "minimax_h3":
-        raise RuntimeError(f"TensorFold MiniMax H3: {path} is not a MiniMax H3 DiT")
-    unet_config["num_layers"] = 0
-    sd = {k[len(prefix):]: f.get(k) for k in f.keys()
-          if k.startswith(prefix) and not k[len(prefix):].startswith("blocks.")}
-    model_config = comfy.model_detection.model_config_from_unet_config(unet_config, sd)
-    load_device = mm.get_torch_device()
-    model_config.set_inference_dtype(torch.bfloat16, torch.bfloat16, device=load_device)
-    model = model_config.get_model(sd, "")
-    model.diffusion_model.blocks = torch.nn.ModuleList(EngineBlock(engine, i) for i in range(len(engine.blocks)))
-    model.diffusion_model.tfvideo_engine = engine
-    engine.comfy_model = model
-    patcher = comfy.model_patcher.CoreModelPatcher(model, load_device=load_device,
-                                                   offload_device=mm.unet_offload_device())
-    model.load_model_weights(sd, "", assign=patcher.is_dynamic())
-    patcher.add_wrapper(comfy.patcher_extension.WrappersMP.DIFFUSION_MODEL, _wrapper(model))
-    patcher.add_callback_with_key(comfy.patcher_extension.CallbacksMP.ON_CLEANUP, "tfvideo", _cleanup(engine))
-    return patcher
+    def detect(self) -> tuple[str, dict]:
+        """(key prefix, ComfyUI unet config) from the checkpoint's key names and shapes alone."""
+
+        import comfy.model_detection as md
+
+        shapes = {k: torch.empty(self.file.shape(k), device="meta") for k in self.file.keys()}
+        prefix = md.unet_prefix_from_state_dict(shapes)
+        if not any(k.startswith(prefix) for k in shapes):
+            prefix = ""                                # bare keys, as ComfyUI's own loader accepts
+        config = md.detect_unet_config(shapes, prefix)
+        if not config or config.get("image_model") != "minimax_h3":
+            raise RuntimeError(f"{self.path}: not a MiniMax H3 DiT checkpoint (ComfyUI detected "
+                               f"{(config or {}).get('image_model')!r})")
+        return prefix, config
+
+    def outside_blocks(self, prefix: str) -> dict:
+        """The checkpoint's tensors outside the DiT blocks, keys without the prefix (the engine owns the blocks)."""
+
+        return {k[len(prefix):]: self.file.get(k) for k in self.file.keys()
+                if k.startswith(prefix) and not k[len(prefix):].startswith("blocks.")}
+
+    def patcher(self, engine):
+        import comfy.model_detection as md
+        import comfy.model_management as mm
+        import comfy.model_patcher as mp
+        import comfy.patcher_extension as pe
+
+        from .minimax_h3 import EngineBlock
+
+        prefix, config = self.detect()
+        config = dict(config, num_layers=0)          # ComfyUI builds no blocks of its own
+        state = self.outside_blocks(prefix)
+        model_config = md.model_config_from_unet_config(config, state)
+        device = mm.get_torch_device()
+        model_config.set_inference_dtype(torch.bfloat16, torch.bfloat16, device=device)
+        model = model_config.get_model(state, "")
+        inner = model.diffusion_model
+        inner.blocks = torch.nn.ModuleList([EngineBlock(engine, i) for i in range(len(engine.blocks))])
+        inner.tfvideo_engine = engine
+        engine.comfy_model = model
+        patcher = mp.CoreModelPatcher(model, load_device=device, offload_device=mm.unet_offload_device())
+        model.load_model_weights(state, "", assign=patcher.is_dynamic())
+        patcher.add_wrapper(pe.WrappersMP.DIFFUSION_MODEL, reject_hook_patches(model))
+        patcher.add_callback_with_key(pe.CallbacksMP.ON_CLEANUP, "tfvideo", end_of_run(engine))
+        return patcher
 
 
-def _wrapper(model):
-    """Around each diffusion-model call: refuse what the engine cannot honour (scheduled hook weight patches)."""
+def reject_hook_patches(model):
+    """Diffusion-model wrapper: scheduled (hook) weight patches change weights per step, which merged NVFP4 weights
+    cannot follow -- refuse them instead of silently ignoring them."""
 
     def wrapper(executor, x, timestep, context, transformer_options={}, **kwargs):
-        patcher = getattr(model, "current_patcher", None)
-        if patcher is not None and getattr(patcher, "hook_patches", None):
-            raise RuntimeError("TensorFold MiniMax H3: hook (scheduled) weight patches are not supported")
+        current = getattr(model, "current_patcher", None)
+        if current is not None and getattr(current, "hook_patches", None):
+            raise RuntimeError("MiniMax H3 on the B200 engine: scheduled (hook) weight patches are not available; "
+                               "apply LoRAs with a regular LoRA loader")
         return executor(x, timestep, context, transformer_options, **kwargs)
+
     return wrapper
 
 
-def _cleanup(engine):
-    """End of a sampling run (ComfyUI's ON_CLEANUP): release the activation buffers, reset the scales."""
+def end_of_run(engine):
+    """ON_CLEANUP callback: the sampling run is over -- drop activation buffers, start the next run on exact scales."""
 
-    def cleanup(patcher):
+    def callback(patcher):
         engine.release_vram()
         engine.end_run()
-    return cleanup
+
+    return callback
 
 
-def _model_files() -> list[str]:
+# ------------------------------------------------------------------------------------------------ the node
+ENGINES = EngineCache()
+
+
+def diffusion_model_files() -> list[str]:
     import folder_paths
 
     return [n for n in folder_paths.get_filename_list("diffusion_models") if n.endswith(".safetensors")]
 
 
 class TFMiniMaxH3Loader:
-    """Load a MiniMax H3 DiT into the B200 engine (converted to NVFP4 once, cached)."""
+    """Loads a MiniMax H3 DiT whose 50 blocks run on the B200 engine (NVFP4 weights, converted once and cached)."""
 
     @classmethod
     def INPUT_TYPES(cls):
-        files = _model_files()
+        files = diffusion_model_files()
         default = next((f for f in files if "minimax_h3" in f), files[0] if files else "")
         return {"required": {"unet_name": (files, {"default": default}),
                              "precision": (PRECISIONS, {"default": "nvfp4"}),
@@ -254,13 +350,13 @@ class TFMiniMaxH3Loader:
         from . import attention as A
 
         spec = check_choices(precision, attention)
-        _install_lora_hook()
+        LoraBridge.install()
         path = folder_paths.get_full_path_or_raise("diffusion_models", unet_name)
-        engine = _engine(path, spec)
+        engine = ENGINES.acquire(path, spec, on_forward)
         engine.attn, engine.attn_name = A.get(attention), attention
-        logging.info(f"[tfvideo] MiniMax H3 engine ready: {spec}, attention {attention}, "
-                     f"{engine.nbytes() / 2**30:.2f} GiB of block weights")
-        return (build_model(path, engine),)
+        log.info("[tfvideo] B200 engine for %s: %s linears, %s attention, %.2f GiB of block weights resident",
+                 unet_name, spec, attention, engine.nbytes() / 2 ** 30)
+        return (ModelShell(path).patcher(engine),)
 
 
 NODE_CLASS_MAPPINGS = {"TFMiniMaxH3Loader": TFMiniMaxH3Loader}

@@ -223,16 +223,20 @@ class MiniMaxH3Engine:
         torch.cuda.empty_cache()
 
     def row_index(self, mod_segments, S: int) -> torch.Tensor:
-        """int32 [S]: each row's modulation row (the segments are the same list object for all 50 blocks)."""
+        """Device int32 [S] mapping every token to the row of the modulation table it uses.
 
-        key = (id(mod_segments), S)
-        if key != self._idx_key:
-            idx = torch.empty(S, dtype=torch.int32)
-            for a, b, row in mod_segments:
-                idx[a:b] = row.cpu().to(torch.int32) if torch.is_tensor(row) else int(row)
-            self._idx = idx.to(self.device, non_blocking=True)
-            self._idx_key = key
-            self._idx_ref = mod_segments
+        ``mod_segments`` lists (first token, end token, row) with ``row`` an int or a per-token tensor.  ComfyUI hands
+        all 50 blocks of one forward the same list object, so the table is built and uploaded once per forward and
+        looked up by the list's identity afterwards; the list is kept referenced so that its id cannot be reused by
+        a different list while the cached table is alive."""
+
+        if (id(mod_segments), S) == self._idx_key:
+            return self._idx
+        host = torch.empty(S, dtype=torch.int32)
+        for first, end, row in mod_segments:
+            host[first:end] = row.cpu().to(torch.int32) if torch.is_tensor(row) else int(row)
+        self._idx = host.to(self.device, non_blocking=True)
+        self._idx_key, self._idx_ref = (id(mod_segments), S), mod_segments
         return self._idx
 
     def rope_table(self, rope_freqs: torch.Tensor, S: int) -> torch.Tensor:
@@ -306,8 +310,9 @@ class MiniMaxH3Engine:
             h = buf.dynamic(cfg, n, self.device)[0]
             N.norm_mod(x, b.norm1, mod, idx, 0, cfg.eps, out=h, slot=self._slot(i, "qkv"))
         if attention is not None:
-            # ComfyUI's attention replacement (e.g. the Model Sparse Attention node): it projects through this
-            # block's facade (EngineBlock.attn) and returns out_proj(attention)
+            # An attention override handed in by ComfyUI (a sparse-attention patch, for instance) owns the whole
+            # attention half: given the normed input it computes qkv, q/k norms, RoPE and attention through
+            # EngineBlock.attn and returns the out-projection's output, which the gate adds to the residual here.
             a = attention(h, rope_freqs=rope_freqs, transformer_options=transformer_options or {})
             K.gate_add(x, a, mod, 0, idx)
             return self._mlp_half(i, b, x, mod, idx, buf, delayed)
@@ -398,7 +403,15 @@ class MiniMaxH3Engine:
         with maybe(T, "gemm_out+gate"):
             lo.gemm(buf.o4, buf.o4sf, n, N.H3Epilogue(kind=N.H3_EPI_GATE_RESID, x=x.data_ptr(), ldx=D,
                                                       mod=mod.data_ptr(), idx=idx.data_ptr(), gate_part=0))
-        return self._mlp_half(i, b, x, mod, idx, buf, delayed)
+        x = self._mlp_half(i, b, x, mod, idx, buf, delayed)
+        if buf.peers is not None and i == len(self.blocks) - 1:
+            # the last block of a Ulysses forward: every barrier of the forward carried the ranks' device status;
+            # a rank whose exchange kernel gave up a wait fails the forward here on every rank (one host read)
+            status = self.sp.failed()
+            if status:
+                raise RuntimeError(f"Ulysses forward failed: a rank's kernel gave up a bounded wait (device status "
+                                   f"{status}); the receive buffers of this forward are incomplete")
+        return x
 
     def _attend(self, q, k, v, S, H, ld, out, ws):
         m = self.attn_mask
@@ -465,7 +478,8 @@ class MiniMaxH3Engine:
 
 
 class _Proj:
-    """A block linear as ComfyUI modules call it (x -> x @ W^T)."""
+    """Calls block ``i``'s linear ``name`` as a plain projection (bf16 [M, K] -> [M, N]) on the NVFP4 GEMM, with
+    the input's own dynamic scale: the form in which an attention override computes qkv and the out-projection."""
 
     def __init__(self, engine, i, name):
         self.engine, self.i, self.name = engine, i, name
@@ -475,6 +489,9 @@ class _Proj:
 
 
 class _Norm:
+    """One of block ``i``'s per-head RMSNorm weights (fp32 [head_dim]) behind a ``.weight`` attribute, read from the
+    engine when asked, so it follows LoRA re-conversions and block swaps; ``eps`` is the norm's epsilon."""
+
     def __init__(self, engine, i, name, eps):
         self.engine, self.i, self.name, self.eps = engine, i, name, eps
 
@@ -484,19 +501,23 @@ class _Norm:
 
 
 class AttnFacade:
-    """What ComfyUI's H3 attention patches read from ``block.attn`` (heads, head_dim, qkv_proj, q/k norms, out_proj),
-    backed by the engine, so patches such as the stock Model Sparse Attention node run on engine blocks."""
+    """``block.attn`` for code written against ComfyUI's own MiniMax H3 block: the attributes an attention override
+    reads (``heads``, ``head_dim``, ``qkv_proj``, ``out_proj``, ``q_norm``, ``k_norm``, ``to_gate_compress``), each
+    resolving to the engine's weights for block ``i``.  The override gets the engine's projections and norms and can
+    run any attention in between, the engine's block-sparse FP8 kernel included."""
 
     def __init__(self, engine, i):
         cfg = engine.cfg
         self.heads, self.head_dim = cfg.heads, cfg.head_dim
         self.qkv_proj, self.out_proj = _Proj(engine, i, "qkv"), _Proj(engine, i, "out")
         self.q_norm, self.k_norm = _Norm(engine, i, "q_norm", cfg.qk_eps), _Norm(engine, i, "k_norm", cfg.qk_eps)
-        self.to_gate_compress = None
+        self.to_gate_compress = None       # MiniMax H3 has no gated attention compression
 
 
 class EngineBlock(torch.nn.Module):
-    """ComfyUI's ``DiTBlock`` call signature on the engine; no parameters of its own (the engine owns them)."""
+    """A stand-in for ComfyUI's MiniMax H3 ``DiTBlock`` in the model's block list: the same forward signature,
+    computed by the engine's block ``i``.  It owns no parameters (the engine keeps every weight), updates ``x`` in
+    place and returns it, and starts the engine's forward (scale policy, LoRA sync) when it is block 0."""
 
     def __init__(self, engine: MiniMaxH3Engine, i: int):
         super().__init__()
@@ -504,17 +525,21 @@ class EngineBlock(torch.nn.Module):
         self.attn = AttnFacade(engine, i)
 
     def forward(self, x, t_emb, mod_segments, rope_freqs, transformer_options={}, attention=None):
-        with _no_malloc_graph():
+        with _outside_comfy_allocation_capture():
             if self.i == 0:
                 sp = self.engine.sp
                 self.engine.begin_forward(x.shape[0] * (1 if sp is None else sp.world), transformer_options)
             return self.engine.block(self.i, x, t_emb, mod_segments, rope_freqs, attention, transformer_options)
 
 
-def _no_malloc_graph():
+def _outside_comfy_allocation_capture():
+    """ComfyUI (dynamic-VRAM mode) records each block's device allocations in order to replay them; the engine keeps
+    its own buffers per sequence length, so its block runs with that recording paused when this ComfyUI offers the
+    switch (``comfy.model_prefetch.pause_malloc_graph``), and as is otherwise."""
+
     try:
-        import comfy.model_prefetch
-        return comfy.model_prefetch.pause_malloc_graph()
+        from comfy.model_prefetch import pause_malloc_graph
     except ImportError:
         import contextlib
         return contextlib.nullcontext()
+    return pause_malloc_graph()

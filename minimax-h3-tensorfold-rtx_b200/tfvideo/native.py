@@ -38,6 +38,7 @@ _SIGS = {
     "h3_version": [],
     "h3_last_error": [C.c_char_p, i32],
     "h3_device_status": [C.POINTER(i32), i32],
+    "h3_status_publish": [vp, vp],
     "h3_sf_tiled_bytes": ([i32, i32], sz),
     "h3_scales_begin": [vp, i32, i32, vp, vp],
     "h3_scales_dynamic": [vp, vp],
@@ -110,6 +111,13 @@ def device_status(reset: bool = False) -> int:
     st = i32(0)
     check(lib().h3_device_status(C.byref(st), int(reset)), "h3_device_status")
     return st.value
+
+
+def status_publish(dst: torch.Tensor) -> None:
+    """dst[0] = max(dst[0], this device's status word), in stream order (fp32 device tensor)."""
+
+    _count(1)
+    check(lib().h3_status_publish(ptr(dst), stream()), "h3_status_publish")
 
 
 def stream() -> int:

@@ -73,11 +73,21 @@ class SequenceParallel:
 
     def barrier(self, device) -> None:
         """In stream order: returns (on the device) once every rank's work before it has finished, so the peer stores
-        that work made are visible to what follows (a one-element all-reduce)."""
+        that work made are visible to what follows (a one-element all-reduce).  The element carries each rank's device
+        status word (max over ranks, sticky): a rank whose kernel gave up a bounded wait -- leaving some receive rows
+        unwritten -- makes ``failed()`` nonzero on every rank, with no host read at the barrier itself."""
 
         if getattr(self, "_flag", None) is None or self._flag.device != torch.device(device):
             self._flag = torch.zeros(1, dtype=torch.float32, device=device)
-        dist.all_reduce(self._flag, group=self.group)
+        if self._flag.is_cuda:
+            N.status_publish(self._flag)
+        dist.all_reduce(self._flag, op=dist.ReduceOp.MAX, group=self.group)
+
+    def failed(self) -> int:
+        """The largest device status any rank published at a barrier so far (0 = none failed); one host read."""
+
+        flag = getattr(self, "_flag", None)
+        return 0 if flag is None else int(flag.item())
 
 
 class QkvExchange:

@@ -17,6 +17,7 @@ from __future__ import annotations
 import hashlib
 import json
 import os
+import re
 import time
 from pathlib import Path
 
@@ -38,44 +39,79 @@ def cache_dir() -> Path:
     return path
 
 
-def key(source: str | Path, spec: str, merge_sig: str = "") -> str:
+def cache_name(source: str | Path, spec: str, lora_sig: str = "") -> str:
+    """File name of a converted engine in the cache: ``<checkpoint stem>.<spec>[.lora].<id>.b200.safetensors``.
+
+    ``id`` digests everything the conversion result depends on -- the checkpoint's resolved path, size and
+    modification time, the precision spec, this file format's version and the LoRA set's signature -- so editing the
+    checkpoint, changing the spec or the LoRAs, or a new format gives a new file instead of a stale one.  The
+    ``b200`` suffix keeps these files apart from the reference's TensorFold caches."""
+
     st = os.stat(source)
-    raw = f"{Path(source).resolve()}|{st.st_size}|{st.st_mtime_ns}|{spec}|{FORMAT}|b200|{merge_sig}"
-    tag = spec.replace(":", "_").replace(",", "_").replace("=", "-") + ("-lora" if merge_sig else "")
-    return f"{Path(source).stem}-{tag}-b200-{hashlib.sha1(raw.encode()).hexdigest()[:10]}"
+    ident = json.dumps({"path": str(Path(source).resolve()), "size": st.st_size, "mtime_ns": st.st_mtime_ns,
+                        "spec": spec, "format": FORMAT, "lora": lora_sig}, sort_keys=True)
+    digest = hashlib.blake2b(ident.encode(), digest_size=6).hexdigest()
+    parts = [Path(source).stem, re.sub(r"[^A-Za-z0-9]+", "-", spec).strip("-")]
+    if lora_sig:
+        parts.append("lora")
+    return ".".join(parts + [digest, "b200"]) + ".safetensors"
 
 
 def _check_spec(spec: str) -> None:
     if spec != "nvfp4":
-        raise ValueError(f"precision {spec!r}: the B200 build converts to 'nvfp4' only")
+        raise ValueError(f"precision {spec!r} is not converted by the B200 build (it converts to 'nvfp4')")
+
+
+class _Progress:
+    """Logs conversion progress at most every ``every`` seconds (converting 50 blocks takes tens of seconds)."""
+
+    def __init__(self, log, total: int, every: float = 10.0):
+        self.log, self.total, self.every = log, total, every
+        self.t0 = self.last = time.perf_counter()
+
+    def step(self, done: int) -> None:
+        now = time.perf_counter()
+        if done == self.total or now - self.last >= self.every:
+            self.log(f"[tfvideo] NVFP4 conversion: block {done} of {self.total}, {now - self.t0:.0f} s")
+            self.last = now
+
+
+def _convert_block(src: Checkpoint, i: int, cfg: Config, slots, device, merge) -> tuple[Block, int]:
+    """Block i with its four linears read in the model's basis, LoRA-merged where ``merge`` patches them, and
+    quantised to NVFP4 on the GPU.  Returns the block and how many of its linears ``merge`` changed."""
+
+    lins, patched = {}, 0
+    for name in LIN_NAMES:
+        full = f"blocks.{i}.{SOURCE[name]}"
+        w = src.linear(full, device)
+        if merge is not None:
+            merged = merge(full, w)
+            if merged is not None:
+                w, patched = merged, patched + 1
+        lins[name] = L.Nvfp4Linear(w.to(torch.bfloat16), slots=slots, slot=4 * i + SLOT[name],
+                                   interleave16=(name == "fc1" and cfg.act == "swiglu"))
+        del w
+    return Block(lins, **src.small(i, device)), patched
 
 
 def convert(source: str | Path, spec: str = "nvfp4", merge=None, device="cuda", log=print,
             attn: str = "auto") -> MiniMaxH3Engine:
-    """``merge(name, w)``: the patched fp32 weight of block linear ``name`` (e.g. ``blocks.3.mlp.fc1``), or None."""
+    """A B200 engine from a ComfyUI-layout MiniMax H3 checkpoint.  ``merge(name, w)`` returns the LoRA-patched fp32
+    weight of block linear ``name`` (e.g. ``blocks.3.mlp.fc1``), or None to keep ``w``."""
 
     _check_spec(spec)
     src = Checkpoint(source)
     cfg = src.config()
     slots = L.new_slots(4 * cfg.layers, device)
-    blocks, merged, t0 = [], 0, time.perf_counter()
+    progress = _Progress(log, cfg.layers)
+    blocks, patched = [], 0
     for i in range(cfg.layers):
-        lins = {}
-        for name in LIN_NAMES:
-            lin_name = f"blocks.{i}.{SOURCE[name]}"
-            w = src.linear(lin_name, device)
-            if merge is not None:
-                patched = merge(lin_name, w)
-                if patched is not None:
-                    w, merged = patched, merged + 1
-            lins[name] = L.Nvfp4Linear(w.to(torch.bfloat16), slots=slots, slot=4 * i + SLOT[name],
-                                       interleave16=(name == "fc1" and cfg.act == "swiglu"))
-            del w
-        blocks.append(Block(lins, **src.small(i, device)))
-        if i % 10 == 9:
-            log(f"[tfvideo] converted {i + 1}/{cfg.layers} blocks ({time.perf_counter() - t0:.0f} s)")
+        block, n = _convert_block(src, i, cfg, slots, device, merge)
+        blocks.append(block)
+        patched += n
+        progress.step(i + 1)
     if merge is not None:
-        log(f"[tfvideo] merged LoRA patches into {merged} block linears")
+        log(f"[tfvideo] LoRA set applied to {patched} of {4 * cfg.layers} block linears")
     return MiniMaxH3Engine(blocks, spec, cfg, device, attn, slots=slots)
 
 
@@ -128,15 +164,22 @@ def load(path: str | Path, device="cuda", attn: str = "auto") -> MiniMaxH3Engine
 
 def load_or_convert(source: str | Path, spec: str = "nvfp4", device="cuda", log=print, merge=None,
                     merge_sig: str = "", attn: str = "auto") -> MiniMaxH3Engine:
+    """The engine for (checkpoint, spec, LoRA set): read from the cache when converted before, else converted now and
+    written to the cache.  A cache file this build cannot read (another format version) is converted again."""
+
     _check_spec(spec)
-    path = cache_dir() / (key(source, spec, merge_sig) + ".safetensors")
+    path = cache_dir() / cache_name(source, spec, merge_sig)
+    engine = None
     if path.is_file():
         t0 = time.perf_counter()
-        engine = load(path, device, attn)
-        log(f"[tfvideo] loaded converted {path.name} in {time.perf_counter() - t0:.1f} s")
-    else:
-        what = " with LoRA" if merge_sig else ""
-        log(f"[tfvideo] converting {Path(source).name} to {spec}{what} (once; cached at {path})")
+        try:
+            engine = load(path, device, attn)
+            log(f"[tfvideo] {path.name}: cached NVFP4 engine read in {time.perf_counter() - t0:.1f} s")
+        except ValueError as e:
+            log(f"[tfvideo] {path.name}: not usable ({e}); converting again")
+    if engine is None:
+        log(f"[tfvideo] converting {Path(source).name} to NVFP4{' with its LoRA set' if merge_sig else ''}; "
+            f"the result is cached as {path}")
         engine = convert(source, spec, merge, device, log, attn)
         save(engine, path)
     engine.source, engine.lora_sig = str(source), merge_sig

@@ -128,3 +128,45 @@ def test_step_graph_replays_match_eager_forwards():
     device_ok()
     assert np.array_equal(got[0], eager[1])
     assert np.array_equal(got[1], eager[2])
+
+
+def test_attention_hook_through_facade_runs_the_block_sparse_kernel():
+    """ComfyUI's attention override (EngineBlock.forward(..., attention=fn), the route the reference keeps for
+    ComfyUI's BlockSparseAttention, tfvideo/minimax_h3.py:285-291): ``fn`` projects through the block's AttnFacade,
+    normalises and rotates q / k, runs the block-sparse FP8 kernel and projects out.  Its block output must equal
+    the engine's own block-sparse path (``engine.attn_mask``) bit for bit: both quantise under the same dynamic
+    scales, run the same kernels, and add the gated residual with the same rounded operations."""
+
+    from tfvideo import attention as A
+    from tfvideo import native as N
+
+    M, cfg, eng, shape, p, x, t_emb, segs, rope = _setup("gelu", 384, 128)
+    S, H, Dh = 384, cfg.heads, cfg.head_dim
+    HD = H * Dh
+    mask = A.TileMask.block_sparse(S, keep=0.5, text_tokens=128, seed=3)
+    rope_t = to_dev(rope, torch.float32).reshape(1, S, 1, 64, 2, 2)
+    te = to_dev(t_emb, torch.float32)
+    blk = M.EngineBlock(eng, 0)
+    fac = blk.attn
+    calls = []
+
+    def sparse_attention(h, rope_freqs, transformer_options):
+        calls.append(tuple(h.shape))
+        qkv = fac.qkv_proj(h)
+        q, k, v = qkv[:, :HD], qkv[:, HD:2 * HD], qkv[:, 2 * HD:]
+        table = rope_freqs.reshape(S, -1, 2, 2).float().contiguous()
+        N.qknorm_rope(q, k, 3 * HD, S, H, 2 * table.shape[1], fac.q_norm.weight, fac.k_norm.weight, table,
+                      fac.q_norm.eps)
+        o = torch.empty((S, HD), dtype=torch.bfloat16, device="cuda")
+        A.fp8_tokens(q, k, v, S, H, 3 * HD, Dh, o, mask=mask)
+        return fac.out_proj(o)
+
+    hooked = to_np(blk(to_dev(x), te, segs, rope_t, attention=sparse_attention))
+    assert calls == [(S, cfg.dim)]
+    eng.end_run()
+    eng.attn_mask = mask
+    own = to_np(blk(to_dev(x), te, segs, rope_t))
+    device_ok()
+    assert np.array_equal(hooked, own)
+    dense = OB.block_forward(shape, p, x, t_emb, segs, rope, linears="bf16", attn="sdpa")
+    assert OO.cosine(hooked, dense) >= 0.99                       # a sparse block stays close to the dense one

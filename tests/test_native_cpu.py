@@ -91,3 +91,24 @@ def test_peer_entry_points_check_their_arguments(lib):
     assert lib.h3_peer_copy(None, 1, None) != 0
     assert lib.h3_peer_alloc(0, None, None) != 0 and "zero" in N.last_error()
     assert lib.h3_peer_open(None, None) != 0
+
+
+def test_noalloc_size_limit_edges(lib):
+    """h3_attn_fp8_noalloc's limit is exact: at H = 40 the largest S whose scratch fits the fixed array (64 MiB minus
+    the 1 KiB alignment step) is found by search, and S + 128 (the next size that needs more scratch) is refused with
+    H3_ERR_SHAPE before any CUDA call; the limit is documented as S * H <= 170,000 (S = 4,096 at H = 40)."""
+
+    from tfvideo import native as N
+
+    cap = (64 << 20) - 1024
+    H = 40
+    S = 4096
+    while N.attn_workspace_bytes(S + 1, H) <= cap:
+        S += 1
+    assert N.attn_workspace_bytes(S, H) <= cap < N.attn_workspace_bytes(S + 128, H)
+    assert 4096 <= S and S * H <= 170_000
+    fake = 1 << 20
+    rc = lib.h3_attn_fp8_noalloc(fake, fake, fake, 3 * H * 128, 128, S + 128, H, fake, H * 128, None)
+    assert rc == -2 and "scratch" in N.last_error() and "h3_attn_fp8_noalloc" in N.last_error()
+    rc = lib.h3_attn_fp8_noalloc(fake, fake, fake, 3 * H * 128, 128, 0, H, fake, H * 128, None)
+    assert rc == -2 and "h3_attn_fp8_noalloc" in N.last_error()

@@ -76,3 +76,55 @@ def test_convert_save_load(tmp_path, monkeypatch, act, ffn):
     with pytest.raises(ValueError):
         store.convert(src, spec="int8")
     device_ok()
+
+
+def test_lora_merge_reconverts_and_caches_per_set(tmp_path, monkeypatch):
+    """store.load_or_convert with ``merge``: only the linears the merge function patches change, each equal to the
+    NVFP4 quantisation of the patched model-basis weight; the LoRA set gets its own cache file and loads back from it;
+    an engine swapped to the merged blocks computes what the merged engine computes."""
+
+    from tfvideo import linear as L
+    from tfvideo import minimax_h3 as M
+    from tfvideo import store
+    from tfvideo.source import Checkpoint
+
+    src = tmp_path / "h3.safetensors"
+    F.write(src, layers=2)
+    cache = tmp_path / "cache"
+    monkeypatch.setenv("TFVIDEO_CACHE", str(cache))
+    quiet = lambda *_: None                                           # noqa: E731
+    base = store.load_or_convert(src, log=quiet)
+    delta = 0.01
+    seen = []
+
+    def merge(name, w):
+        seen.append(name)
+        return w + delta if name == "blocks.1.mlp.fc1" else None
+
+    sig = "abc123@0.7500"
+    lora = store.load_or_convert(src, log=quiet, merge=merge, merge_sig=sig)
+    assert len(seen) == 8 and lora.lora_sig == sig
+    w = Checkpoint(src).linear("blocks.1.mlp.fc1", "cuda")
+    direct = L.Nvfp4Linear((w + delta).to(torch.bfloat16))
+    assert torch.equal(lora.blocks[1].lins["fc1"].codes, direct.codes)
+    assert torch.equal(lora.blocks[1].lins["fc1"].sf, direct.sf)
+    assert not torch.equal(lora.blocks[1].lins["fc1"].codes, base.blocks[1].lins["fc1"].codes)
+    for i, name in ((0, "fc1"), (1, "qkv"), (1, "fc2")):
+        assert torch.equal(lora.blocks[i].lins[name].codes, base.blocks[i].lins[name].codes)
+    files = sorted(p.name for p in cache.iterdir())
+    assert len(files) == 2 and sum(".lora." in f for f in files) == 1
+    seen.clear()
+    again = store.load_or_convert(src, log=quiet, merge=merge, merge_sig=sig)   # from the cache: no merge calls
+    assert seen == [] and torch.equal(again.blocks[1].lins["fc1"].codes, direct.codes)
+
+    S, rot = 128, 128
+    x = to_dev(bf16_array((S, base.cfg.dim), 9))
+    te = to_dev(np.random.RandomState(4).randn(2, base.cfg.t_dim).astype(np.float32), torch.float32)
+    segs = [(0, S, 1)]
+    rope_t = to_dev(OB.rope_table(S, rot), torch.float32).reshape(1, S, 1, rot // 2, 2, 2)
+    base.replace_blocks(lora.blocks, sig, slots=lora.slots)
+    a = M.EngineBlock(base, 0)(x.clone(), te, segs, rope_t)
+    lora.end_run()
+    b = M.EngineBlock(lora, 0)(x.clone(), te, segs, rope_t)
+    assert torch.equal(a, b)
+    device_ok()

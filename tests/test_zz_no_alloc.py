@@ -27,12 +27,15 @@ def _cos(a: torch.Tensor, b: torch.Tensor) -> float:
     return float(a @ b / (a.norm() * b.norm()))
 
 
-def test_noalloc_attention_matches_allocating_entry_point():
+@pytest.mark.parametrize("S,H", [(1000, 4), (4096, 40)], ids=["small", "limit_example"])
+def test_noalloc_attention_matches_allocating_entry_point(S, H):
+    """Two calls in a row through the C ABI against h3_attn_fp8 on the same inputs; (4096, 40) is the documented
+    example of a size at the array's limit (its scratch fills most of the 64 MiB)."""
+
     need_gpu()
     from tfvideo import native as N
 
     lib = N.lib()
-    S, H = 1000, 4
     HD = H * 128
     g = torch.Generator(device="cuda").manual_seed(7)
     qkv = torch.randn(S, 3 * HD, generator=g, device="cuda").to(torch.bfloat16)
