@@ -400,6 +400,8 @@ def micro(a) -> None:
 
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
     g = torch.Generator(device="cuda").manual_seed(0)
+    if a.micro == "elem":
+        return micro_elem(a)
     if a.micro == "attn":
         S, H = a.seq, a.heads
         qkv = dev_qkv(S, H, seed=S).view(S, 3 * H * 128)
@@ -451,6 +453,50 @@ def micro(a) -> None:
           flush=True)
 
 
+def micro_elem(a) -> None:
+    """The HBM-bound kernels of a block alone at S tokens (BASELINE shapes), each launch timed with CUDA events after
+    an L2 flush; rates are algorithmic bytes (read + written once) over the measured copy bandwidth."""
+
+    from tfvideo import linear as L
+    from tfvideo import native as N
+    from tfvideo.synthetic import dev_activations
+
+    S, D, H = a.seq, 5120, a.heads
+    pk, src = peaks()
+    hbm = pk["hbm_gbs"]
+    g = torch.Generator(device="cuda").manual_seed(1)
+    x = dev_activations(S, D, seed=3)
+    w = 1 + 0.02 * torch.randn(D, generator=g, device="cuda")
+    mod = 0.1 * torch.randn(4, 6, D, generator=g, device="cuda")
+    idx = torch.randint(0, 4, (S,), generator=g, device="cuda", dtype=torch.int32)
+    slots = L.new_slots(1, "cuda")
+    slots[0, 1] = float(x.float().abs().amax()) / 2688.0
+    codes = torch.empty(S, D // 2, dtype=torch.uint8, device="cuda")
+    sf = torch.zeros(N.sf_tiled_bytes(S, D), dtype=torch.uint8, device="cuda")
+    yb = torch.empty_like(x)
+    qkv = dev_activations(S, 3 * H * 128, seed=4)
+    rope = rope_3d(S).cuda().reshape(S, -1, 2, 2).contiguous()
+    qw, kw = (1 + 0.02 * torch.randn(128, generator=g, device="cuda") for _ in range(2))
+    HD = H * 128
+    sp = N.slot_ptr(slots, 0)
+    cases = {
+        "norm_mod+nvfp4 (delayed-scale forward)": (lambda: N.norm_mod(x, w, mod, idx, 0, 1e-5, codes=codes, sf=sf,
+                                                                      slot=sp), S * D * (2 + 0.5625)),
+        "norm_mod bf16 + amax (first forward)": (lambda: N.norm_mod(x, w, mod, idx, 0, 1e-5, out=yb, slot=sp),
+                                                 S * D * 4),
+        "nvfp4_quant [S, 5120]": (lambda: N.nvfp4_quant(x, codes, sf, g_ptr=sp + 4, amax_ptr=sp), S * D * 2.5625),
+        "qknorm_rope (q, k in place)": (lambda: N.qknorm_rope(qkv[:, :HD], qkv[:, HD:2 * HD], 3 * HD, S, H, 128, qw,
+                                                             kw, rope, 1e-5), S * 2 * HD * 4),
+    }
+    flush = Flush()
+    for name, (run, nbytes) in cases.items():
+        ms = time_launches(run, reps=a.steps, warmup=max(a.warmup, 1), flush=flush)
+        gbs = nbytes / ms / 1e6
+        print(json.dumps({"micro": name, "S": S, "us": round(ms * 1e3, 1), "gb_s": round(gbs, 1),
+                          "frac": round(gbs / hbm, 4), "peak_note": f"{src} copy bandwidth {hbm} GB/s"}), flush=True)
+    print(json.dumps({"device_status": N.device_status()}), flush=True)
+
+
 # ------------------------------------------------------------------------------------------------ GPU leg
 def main():
     ap = argparse.ArgumentParser()
@@ -464,7 +510,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the parity probe and the config sweeps")
-    ap.add_argument("--micro", choices=["attn", "gemm"], help="time one op alone (BASELINE configs 1 / 2)")
+    ap.add_argument("--micro", choices=["attn", "gemm", "elem"],
+                    help="time one op alone (BASELINE configs 1 / 2; elem: the HBM-bound kernels)")
     ap.add_argument("--heads", type=int, default=40)
     ap.add_argument("--mnk", default="37760,15360,5120", help="--micro gemm: M,N,K")
     ap.add_argument("--epi", default="store", choices=["store", "gate", "act_q"])
@@ -533,6 +580,12 @@ def main():
     eng.timer = None
     ms = st.elapsed_time(en) / a.steps
     stages = timer.summary()
+    stage_ranks = None
+    if world > 1:   # every rank's own stage times: the exchange waits show which rank the others wait for
+        mine = {k: round(v["ms"] / a.steps, 3) for k, v in stages.items()}
+        every = [None] * world
+        torch.distributed.all_gather_object(every, mine)
+        stage_ranks = {k: [r.get(k) for r in every] for k in mine}
     status = N.device_status()
     finite = bool(torch.isfinite(x).all())
     t = torch.tensor([ms], device="cuda")
@@ -641,6 +694,7 @@ def main():
                            "l2": "inputs larger than L2 (8.9 GB weights + activations per step); sweeps flush L2 "
                                  "before each timed launch"},
                 "stages_ms_per_step": {k: round(v["ms"] / a.steps, 3) for k, v in stages.items()},
+                "stages_ms_per_step_by_rank": stage_ranks,
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
                 "clocks": clocks.summary(), "device_status": status, "finite": finite, "parity": parity,
                 "configs": configs}

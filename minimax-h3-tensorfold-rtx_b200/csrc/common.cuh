@@ -203,6 +203,77 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8])
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// ------------------------------------------------------------------------------------------------ CTA pairs (cta_group::2)
+// A cluster of two CTAs on two SMs sharing one MMA: rank 0 (the leader) issues every tcgen05.mma / tcgen05.cp of the
+// pair; each CTA holds its half of the A rows and of the B rows in its own shared memory and its half of the
+// accumulator rows in its own TMEM (the same columns in both).  No load here multicasts: each CTA loads its own data.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// every thread of both CTAs: orders prior shared-memory writes (barrier inits) before the peer's accesses
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// the shared::cluster address of this CTA's shared variable at `p` as seen in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+// one arrival on an mbarrier of another CTA of the cluster (cluster address from cluster_addr)
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+// warp-wide: a 2-D tile into this CTA's shared memory whose completed bytes count on the leader's barrier
+// (bar_cluster: the leader's mbarrier as a cluster address)
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t.reg .b32 rx;\n\t" H3_ELECT
+      "@e cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];\n\t}" ::"r"(smem_u32(smem_dst)), "l"(map), "r"(x), "r"(y), "r"(bar_cluster)
+      : "memory");
+}
+// TMEM allocation of the pair (one warp in each CTA executes it; the same columns in both CTAs)
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_result)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// warp-wide (leader): completion of the pair's MMAs -> one arrival on the barrier at this shared offset in each CTA of
+// `mask` (bit r: CTA rank r)
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar, uint16_t mask) {
+  asm volatile("{\n\t.reg .pred e;\n\t.reg .b32 rx;\n\t" H3_ELECT
+               "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+               "\n\t}" ::"r"(smem_u32(bar)), "h"(mask)
+               : "memory");
+}
+// warp-wide (leader): D (+)= A x B^T over the pair: M = 256 (rows 0-127 from the leader's A tile, 128-255 from the
+// peer's at the same offset), N split the same way over the two B tiles; NVFP4 with UE4M3 scales from TMEM
+__device__ __forceinline__ void mma_nvfp4_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 rx;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t" H3_ELECT
+      "@e tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+// warp-wide (leader): tcgen05.cp 32x128b.warpx4 in both CTAs of the pair, each from its own shared memory
+__device__ __forceinline__ void tmem_cp_pair_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("{\n\t.reg .pred e;\n\t.reg .b32 rx;\n\t" H3_ELECT
+               "@e tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;\n\t}" ::"r"(taddr), "l"(sdesc)
+               : "memory");
+}
+
 // ------------------------------------------------------------------------------------------------ UMMA descriptors
 // Shared-memory matrix descriptor (sm_100 format): start address >> 4 in bits 0-13, leading byte offset >> 4 in
 // 16-29, stride byte offset >> 4 in 32-45, version 1 in 46-47, base offset 0, layout type in 61-63.
@@ -292,6 +363,27 @@ __device__ __forceinline__ uint32_t quant_group16(const float (&v)[16], float in
   codes[1] = e2m1x8(xs + 8);
   return sf;
 }
+
+// quant_group16 with 1 / e4m3(scale) read from `rcp` (rcp[b] = the IEEE quotient 1 / max(e4m3(b), 1e-30) for the
+// scale bytes 0 .. 126 the saturating conversion can produce): the same codes, one division fewer per group.
+__device__ __forceinline__ uint32_t quant_group16_tab(const float (&v)[16], float inv_g, uint32_t (&codes)[2],
+                                                      const float* rcp) {
+  float xs[16];
+  float gmax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    xs[i] = __fmul_rn(v[i], inv_g);
+    gmax = fmaxf(gmax, fabsf(xs[i]));
+  }
+  uint32_t sf = e4m3(__fdiv_rn(gmax, 6.0f));
+  const float inv = rcp[sf];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) xs[i] = __fmul_rn(xs[i], inv);
+  codes[0] = e2m1x8(xs);
+  codes[1] = e2m1x8(xs + 8);
+  return sf;
+}
+__device__ __forceinline__ float e4m3_rcp_entry(uint32_t b) { return __fdiv_rn(1.0f, fmaxf(e4m3_to_f32(b), 1e-30f)); }
 
 // Byte offset of scale (row r, group k16) in the tiled scale layout the GEMM reads (128-row x 4-group atoms of 512
 // bytes, [row block][group block] order; inside an atom (r % 32) * 16 + (r / 32 % 4) * 4 + k16 % 4).

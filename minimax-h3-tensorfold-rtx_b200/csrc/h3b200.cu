@@ -73,6 +73,22 @@ int make_map_u8(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows
   return H3_OK;
 }
 
+// A tiled scale buffer (h3_sf_tiled_bytes layout) as rows of 2048 bytes -- the scales of 128 matrix rows for one
+// 256-element K tile, contiguous -- read one row per box (256 eight-byte elements, no swizzle).
+int make_map_sf_rows(CUtensorMap* map, const void* base, uint64_t rows, const char* what) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(H3_ERR_CUDA, "%s: cuTensorMapEncodeTiled unavailable from the driver", what);
+  cuuint64_t dims[2] = {256, rows};
+  cuuint64_t strides[1] = {2048};
+  cuuint32_t box[2] = {256, 1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(H3_ERR_CUDA, "%s: cuTensorMapEncodeTiled (scales) failed (%d)", what, (int)r);
+  return H3_OK;
+}
+
 // Opt a kernel into more than 48 KB of dynamic shared memory once per device.
 template <typename K>
 int smem_optin(K kernel, int bytes, unsigned* done_mask, const char* what) {
@@ -86,6 +102,9 @@ int smem_optin(K kernel, int bytes, unsigned* done_mask, const char* what) {
 }
 
 unsigned g_optin_attn[2] = {0, 0};   // [NT - 1]
+#ifndef H3_GEMM_PAIR
+#define H3_GEMM_PAIR 0
+#endif
 
 // Streaming multiprocessors of the current device (cached per device).
 int num_sms() {
@@ -111,6 +130,42 @@ int launch_gemm_t(int grid, const CUtensorMap& ta, const CUtensorMap& tb, const 
   if (rc) return rc;
   gemm_nvfp4_kernel<BN, EPI><<<grid, kGemmThreads(EPI), GemmSmem<BN>::TOTAL, st>>>(ta, tb, p);
   return H3_OK;
+}
+
+unsigned g_optin_pair[5] = {};
+
+// CTA pairs: a cluster of two CTAs per output tile (tcgen05 cta_group::2).
+template <int EPI>
+int launch_gemm_pair_t(int grid, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tsa,
+                       const CUtensorMap& tsb, const GemmArgs& p, cudaStream_t st) {
+  int rc = smem_optin(gemm_nvfp4_pair_kernel<EPI>, GemmPairSmem::TOTAL, &g_optin_pair[EPI], "h3_gemm_nvfp4");
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kGemmThreads(EPI));
+  cfg.dynamicSmemBytes = GemmPairSmem::TOTAL;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_nvfp4_pair_kernel<EPI>, ta, tb, tsa, tsb, p);
+  if (e != cudaSuccess) return fail(H3_ERR_CUDA, "h3_gemm_nvfp4: cluster launch: %s", cudaGetErrorString(e));
+  return H3_OK;
+}
+
+int launch_gemm_pair(int epi, int grid, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tsa,
+                     const CUtensorMap& tsb, const GemmArgs& p, cudaStream_t st) {
+  switch (epi) {
+    case H3_EPI_STORE: return launch_gemm_pair_t<H3_EPI_STORE>(grid, ta, tb, tsa, tsb, p, st);
+    case H3_EPI_GATE_RESID: return launch_gemm_pair_t<H3_EPI_GATE_RESID>(grid, ta, tb, tsa, tsb, p, st);
+    case H3_EPI_ACT_BF16: return launch_gemm_pair_t<H3_EPI_ACT_BF16>(grid, ta, tb, tsa, tsb, p, st);
+    case H3_EPI_ACT_Q: return launch_gemm_pair_t<H3_EPI_ACT_Q>(grid, ta, tb, tsa, tsb, p, st);
+    default: return launch_gemm_pair_t<H3_EPI_STORE_PEERS>(grid, ta, tb, tsa, tsb, p, st);
+  }
 }
 
 int launch_gemm(int BN, int epi, int grid, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& p,
@@ -455,9 +510,20 @@ int h3_gemm_nvfp4(const uint8_t* a_codes, const uint8_t* a_sf, const H3ScaleSlot
       return fail(H3_ERR_ARG, "h3_gemm_nvfp4: unknown epilogue %d", epi->kind);
   }
   CUtensorMap ta, tb;
-  const int BN = (N % 256 == 0) ? 256 : 128;
   int rc = make_map_u8(&ta, a_codes, K / 2, M, K / 2, 128, 128, "h3_gemm_nvfp4(A)");
   if (rc) return rc;
+  if (H3_GEMM_PAIR && N % 256 == 0 && num_sms() >= 2) {   // CTA pairs over 256 x 256 tiles
+    CUtensorMap tsa, tsb;
+    if ((rc = make_map_u8(&tb, b_codes, K / 2, N, K / 2, 128, 128, "h3_gemm_nvfp4(B)"))) return rc;
+    if ((rc = make_map_sf_rows(&tsa, a_sf, (uint64_t)((M + 127) / 128) * (K / 256), "h3_gemm_nvfp4(A scales)")))
+      return rc;
+    if ((rc = make_map_sf_rows(&tsb, b_sf, (uint64_t)(N / 128) * (K / 256), "h3_gemm_nvfp4(B scales)"))) return rc;
+    const int tiles = (N / 256) * ((M + 255) / 256);
+    const int pairs = tiles < num_sms() / 2 ? tiles : num_sms() / 2;
+    if ((rc = launch_gemm_pair(epi->kind, 2 * pairs, ta, tb, tsa, tsb, p, S_(stream)))) return rc;
+    return check_launch("h3_gemm_nvfp4");
+  }
+  const int BN = (N % 256 == 0) ? 256 : 128;
   rc = make_map_u8(&tb, b_codes, K / 2, N, K / 2, 128, BN, "h3_gemm_nvfp4(B)");
   if (rc) return rc;
   const int tiles = (N / BN) * ((M + 127) / 128);

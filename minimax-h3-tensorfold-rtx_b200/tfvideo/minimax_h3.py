@@ -352,9 +352,10 @@ class MiniMaxH3Engine:
                     if j + 1 < len(parts):
                         side.wait_stream(torch.cuda.current_stream(self.device))
                         N.peer_copy(xq.copies(r0, r1), side.cuda_stream)
-            with maybe(T, "exchange"):
+            with maybe(T, "exchange_push"):
                 N.peer_push(xq.copies(*parts[-1]))
                 torch.cuda.current_stream(self.device).wait_stream(side)
+            with maybe(T, "exchange_barrier"):
                 self.sp.barrier(self.device)
             qa = buf.qkv_all.view(S, 3 * Hl * Dh)
             q, k, v = qa[:, :Hl * Dh], qa[:, Hl * Dh:2 * Hl * Dh], qa[:, 2 * Hl * Dh:]
@@ -366,7 +367,7 @@ class MiniMaxH3Engine:
                     raise ValueError(f"attn_mask is for S={m.S}, the sequence has S={S}")
                 N.attn_fp8_peers(q, k, v, 3 * Hl * Dh, Dh, S, Hl, op.ptrs, rank, Hl * Dh, ws,
                                  kv_ptr=None if m is None else m.kv_ptr, kv_idx=None if m is None else m.kv_idx)
-            with maybe(T, "exchange"):
+            with maybe(T, "exchange_barrier"):
                 self.sp.barrier(self.device)
             src = dict(x=buf.o_recv, R=n, K=HD, ldx=Hl * Dh, cblk=Hl * Dh, blk_stride=n * Hl * Dh)
         else:
