@@ -1,9 +1,11 @@
 """Build libh3b200.so (the C-ABI library of the sm_100a kernels) in-tree.
 
-    python minimax-h3-tensorfold-rtx_b200/build.py [--force] [--verbose]
+    python minimax-h3-tensorfold-rtx_b200/build.py [--force] [--verbose] [--define NAME=VALUE ...] [--out PATH]
 
 nvcc cross-compiles for sm_100a without a GPU.  The output lands in
-minimax-h3-tensorfold-rtx_b200/tfvideo/_native/libh3b200.so, next to the Python package that loads it.
+minimax-h3-tensorfold-rtx_b200/tfvideo/_native/libh3b200.so, next to the Python package that loads it.  --define
+and --out build a variant elsewhere (e.g. --define H3_GEMM_PAIR=1 for the CTA-pair GEMM), which tfvideo.native loads
+when the H3B200_LIB environment variable names it.
 """
 
 from __future__ import annotations
@@ -41,27 +43,30 @@ def stale() -> bool:
     return any(p.stat().st_mtime > t for p in sources())
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and not stale():
+def build(force: bool = False, verbose: bool = False, defines: tuple[str, ...] = (), out: Path | None = None) -> Path:
+    target = Path(out) if out else OUT
+    if not force and not defines and out is None and not stale():
         return OUT
-    OUT.parent.mkdir(parents=True, exist_ok=True)
-    tmp = OUT.with_suffix(".so.tmp")
+    target.parent.mkdir(parents=True, exist_ok=True)
+    tmp = target.with_suffix(".so.tmp")
     cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC,-O2",
            f"-I{INCLUDE}", f"-I{CSRC}", "--expt-relaxed-constexpr", "-Xptxas", "-v" if verbose else "-O3",
-           "-o", str(tmp), str(CSRC / "h3b200.cu")]
+           *[f"-D{d}" for d in defines], "-o", str(tmp), str(CSRC / "h3b200.cu")]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         sys.stderr.write(r.stdout + r.stderr)
         raise RuntimeError("nvcc failed building libh3b200.so")
     if verbose:
         sys.stderr.write(r.stderr)
-    os.replace(tmp, OUT)
-    return OUT
+    os.replace(tmp, target)
+    return target
 
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
+    ap.add_argument("--define", action="append", default=[], help="NAME=VALUE passed to nvcc as -DNAME=VALUE")
+    ap.add_argument("--out", default=None, help="write the library here instead of tfvideo/_native")
     a = ap.parse_args()
-    print(build(a.force, a.verbose))
+    print(build(a.force, a.verbose, tuple(a.define), a.out))

@@ -74,24 +74,9 @@ struct NormModArgs {
   H3ScaleSlot* slot;      // nullable: amax of y is accumulated here; act is the quantiser's global scale
 };
 
-#ifndef H3_NM_UNROLL
-#define H3_NM_UNROLL 1
-#endif
-#ifndef H3_NM_RCP_TABLE
-#define H3_NM_RCP_TABLE 0
-#endif
-#define H3_PRAGMA_(x) _Pragma(#x)
-#define H3_PRAGMA(x) H3_PRAGMA_(x)
 __global__ void __launch_bounds__(256) norm_mod_kernel(NormModArgs a) {
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-#if H3_NM_RCP_TABLE
-  // 1 / max(e4m3(b), 1e-30) for every scale byte b the quantiser can produce (0 .. 126): the same IEEE division as the
-  // per-group one it replaces, so the codes are unchanged
-  __shared__ float rcp_tab[128];
-  if (threadIdx.x < 128) rcp_tab[threadIdx.x] = e4m3_rcp_entry(threadIdx.x);
-  __syncthreads();
-#endif
   if (row >= a.S) return;
   const int nit = (a.D + 255) >> 8;
   const __nv_bfloat16* xr = a.x + (size_t)row * a.ldx;
@@ -122,7 +107,7 @@ __global__ void __launch_bounds__(256) norm_mod_kernel(NormModArgs a) {
   float amax = 0.f;
   const int kgroups = a.D >> 4;
   const bool sf_words = (kgroups & 3) == 0;   // every 4-group quad lies inside the row
-H3_PRAGMA(unroll H3_NM_UNROLL)
+#pragma unroll 1
   for (int it = 0; it < nit; ++it) {
     int c = it * 256 + lane * 8;
     bool ok = c < a.D;
@@ -163,11 +148,7 @@ H3_PRAGMA(unroll H3_NM_UNROLL)
       }
       gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 1));
       uint32_t sfb = e4m3(__fdiv_rn(gm, 6.0f));
-#if H3_NM_RCP_TABLE
-      float inv = rcp_tab[sfb];
-#else
       float inv = __fdiv_rn(1.0f, fmaxf(e4m3_to_f32(sfb), 1e-30f));
-#endif
 #pragma unroll
       for (int j = 0; j < 8; ++j) xs[j] = __fmul_rn(xs[j], inv);
       uint32_t cw = e2m1x8(xs);
@@ -211,19 +192,15 @@ struct QuantArgs {
   float* amax;
 };
 
-#ifndef H3_Q_RCP_TABLE
-#define H3_Q_RCP_TABLE 0
-#endif
 __global__ void __launch_bounds__(256) nvfp4_quant_kernel(QuantArgs a) {
   const int groups = a.K >> 4;
-#if H3_Q_RCP_TABLE
-  // per block: the global reciprocal and the 1 / e4m3(scale) table (the same IEEE divisions each thread made)
+  // per block: the global scale's reciprocal and 1 / e4m3(scale) for every scale byte, the same IEEE divisions each
+  // group made before (170 against 176 us at [37,760, 5,120])
   __shared__ float rcp_tab[128];
   __shared__ float s_inv_g;
   if (threadIdx.x < 128) rcp_tab[threadIdx.x] = e4m3_rcp_entry(threadIdx.x);
   if (threadIdx.x == 0) s_inv_g = __fdiv_rn(1.0f, a.g_ptr ? *a.g_ptr : a.g);
   __syncthreads();
-#endif
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   float am = 0.f;
   uint32_t sfb = 0;
@@ -243,12 +220,7 @@ __global__ void __launch_bounds__(256) nvfp4_quant_kernel(QuantArgs a) {
       am = fmaxf(am, fmaxf(fabsf(v[2 * j]), fabsf(v[2 * j + 1])));
     }
     uint32_t cw[2];
-#if H3_Q_RCP_TABLE
     sfb = quant_group16_tab(v, s_inv_g, cw, rcp_tab);
-#else
-    const float g = a.g_ptr ? *a.g_ptr : a.g;
-    sfb = quant_group16(v, __fdiv_rn(1.0f, g), cw);
-#endif
     *reinterpret_cast<uint2*>(a.codes + (size_t)r * (a.K >> 1) + (c >> 1)) = make_uint2(cw[0], cw[1]);
     off = a.sf_tiled ? sf_tiled_offset(r, k16, groups) : (size_t)r * groups + k16;
     if ((groups & 3) != 0) a.sf[off] = (uint8_t)sfb;

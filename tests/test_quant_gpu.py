@@ -88,10 +88,12 @@ def test_norm_mod_bit_exact(S, D, R, part):
     device_ok()
 
 
-@pytest.mark.parametrize("S,D", [(5, 256), (300, 5120), (129, 5376)])
-def test_fused_norm_mod_quant_bit_exact(S, D):
+@pytest.mark.parametrize("S,D,segments", [(5, 256, False), (300, 5120, False), (129, 5376, False),
+                                           (1000, 5120, True), (77, 768, True)])
+def test_fused_norm_mod_quant_bit_exact(S, D, segments):
     """norm_mod + NVFP4 in one kernel (the delayed-scale path): codes / scales equal the oracle's quantisation of the
-    oracle's norm_mod output, and the slot's amax equals max |y|."""
+    oracle's norm_mod output, and the slot's amax equals max |y|.  segments: contiguous runs of one modulation row
+    (as in a video's token segments), else a random modulation row per token."""
 
     from tfvideo import linear as L
     from tfvideo import native as N
@@ -101,6 +103,8 @@ def test_fused_norm_mod_quant_bit_exact(S, D):
     w = (1 + 0.02 * rs.randn(D)).astype(np.float32)
     mod = (0.1 * rs.randn(4, 6, D)).astype(np.float32)
     idx = rs.randint(0, 4, size=S).astype(np.int32)
+    if segments:
+        idx = np.sort(idx).astype(np.int32)
     ref_y = OO.norm_mod(x, w, mod, 1, idx, 1e-5)
     g = ON.global_scale(float(np.abs(ref_y).max()) * 1.5)
     slots = L.new_slots(1, "cuda")
