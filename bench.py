@@ -508,11 +508,15 @@ def main():
     ap.add_argument("--layers", type=int, default=50)
     ap.add_argument("--cpu-rows", type=int, default=512)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-full-block", action="store_true",
+                    help="also time one whole S-token block on the host CPU (minutes), beside the per-row sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the parity probe and the config sweeps")
     ap.add_argument("--micro", choices=["attn", "gemm", "elem"],
                     help="time one op alone (BASELINE configs 1 / 2; elem: the HBM-bound kernels)")
     ap.add_argument("--heads", type=int, default=40)
+    ap.add_argument("--qkv-parts", type=int, default=None,
+                    help="Ulysses: row parts of the qkv GEMM whose exchange overlaps the next part (engine default)")
     ap.add_argument("--mnk", default="37760,15360,5120", help="--micro gemm: M,N,K")
     ap.add_argument("--epi", default="store", choices=["store", "gate", "act_q"])
     ap.add_argument("--sparse", action="store_true",
@@ -545,6 +549,8 @@ def main():
     if a.sparse:
         from tfvideo import attention as A
         eng.attn_mask = A.TileMask.block_sparse(S)
+    if a.qkv_parts:
+        eng.qkv_parts = a.qkv_parts
     x0 = activations(S, cfg.dim)[t0:t0 + n].cuda()
     t_emb = torch.randn(2, cfg.t_dim, generator=torch.Generator().manual_seed(3)).cuda()
     segs = mod_segments(S)
@@ -661,6 +667,7 @@ def main():
                                "peak_note": f"4 x {src} bf16 sustained: dense NVFP4 = 4 x bf16 on B200; "
                                             f"frac_nominal against the 9 PF/s dense NVFP4 figure"}}
 
+    eng_parts = eng.qkv_parts
     # ---- single GPU only: parity at the timed shape, the config-1 / config-2 sweeps and the real-H3 block
     parity = configs = None
     if world == 1 and not a.no_extra:
@@ -680,6 +687,10 @@ def main():
                "config0_block_seconds": c0["seconds"],
                "config0": "one full block, 4,096 tokens, D 5120, 40 x 128 heads, GELU 20480, NVFP4 fake-quant, timed "
                           "outright", **cpu_info()}
+        if a.cpu_full_block:   # the sample's check: one whole 37,760-token block (minutes, ~30 GB of host memory)
+            full = cpu_block(S, S)
+            cpu["config3_full_block_seconds"] = full["seconds"]
+            cpu["config3_full_block_x50"] = full["seconds"] * a.layers
     if rank == 0:
         line = {"metric": METRIC, "value": ms / 1e3, "unit": "s/step", "n_gpus": world, "steps": a.steps,
                 "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "strong",
@@ -688,7 +699,8 @@ def main():
                 "config": {"workload": "config 3/4: 50-block H3-shaped DiT step, 37,760 tokens (512/1680/496/35072), "
                                        "D=5120, 40x128 heads, GELU-tanh FFN 20480, NVFP4 W4A4 + FP8 attention",
                            "global_batch": 1, "seq_len": S, "layers": cfg.layers,
-                           "parallelism": "single GPU" if world == 1 else f"ulysses sp{world} (token-sharded)",
+                           "parallelism": ("single GPU" if world == 1 else
+                                           f"ulysses sp{world} (token-sharded, qkv exchange in {eng_parts} row parts)"),
                            "attention_mask": (f"block-sparse 128x128 tiles, {density:.4f} kept (seed 4)"
                                               if a.sparse else "dense"),
                            "l2": "inputs larger than L2 (8.9 GB weights + activations per step); sweeps flush L2 "

@@ -157,6 +157,7 @@ class MiniMaxH3Engine:
         self.clipped = torch.zeros((), dtype=torch.int32, device=self.device)
         self.timer = None                  # a profiling.StageTimer to time each stage of each block
         self.attn_mask = None              # attention.TileMask: block-sparse FP8 attention when set
+        self.qkv_parts = 4                 # Ulysses: row parts of the qkv GEMM (all but the last sent by copy engines)
 
     # ------------------------------------------------------------------ construction
     @classmethod
@@ -339,9 +340,9 @@ class MiniMaxH3Engine:
             Hl, rank = H // world, self.sp.rank
             qp, op = buf.peers
             xq = QkvExchange(rank, world, n, 3 * Hl * Dh, buf.qkv.element_size(), qp.ptrs, buf.qkv.data_ptr())
-            # two row halves: the first half's blocks leave on the copy engines (no SMs) while the GEMM computes
-            # the second; the second half's go by the push kernel once the GEMM has freed the SMs
-            parts = xq.row_parts()
+            # row parts: each part's blocks but the last leave on the copy engines (no SMs) while the GEMM computes
+            # the next part; the last part's go by the push kernel once the GEMM has freed the SMs
+            parts = xq.row_parts(parts=self.qkv_parts)
             side = self.__dict__.setdefault("_side_stream", torch.cuda.Stream(device=self.device))
             with maybe(T, "gemm_qkv"):
                 for j, (r0, r1) in enumerate(parts):

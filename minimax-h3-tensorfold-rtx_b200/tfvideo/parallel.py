@@ -104,11 +104,15 @@ class QkvExchange:
         self.row = row_elems * elem_bytes   # bytes of one token's row in a receive buffer (3 Hr Dh elements)
         self.recv, self.send = recv, send
 
-    def row_parts(self, tile: int = 128) -> list[tuple[int, int]]:
-        """The GEMM's two row halves, split at a multiple of ``tile`` rows (one part when n is below two tiles)."""
+    def row_parts(self, tile: int = 128, parts: int = 2) -> list[tuple[int, int]]:
+        """The qkv GEMM's row parts: up to ``parts`` contiguous ranges of near-equal length, split at multiples of
+        ``tile`` rows (the last part takes the ragged end; one part when n is below two tiles).  Every part but the
+        last goes to the other ranks by the copy engines while the GEMM computes the next part."""
 
-        m1 = (self.n // 2) // tile * tile
-        return [(0, m1), (m1, self.n)] if m1 > 0 else [(0, self.n)]
+        tiles = self.n // tile
+        k = max(1, min(parts, tiles))
+        cuts = [(tiles * j // k) * tile for j in range(k)] + [self.n]
+        return [(a, b) for a, b in zip(cuts, cuts[1:]) if b > a]
 
     def bases(self, m0: int, M: int) -> list[int]:
         """The epilogue's base for each rank, for a launch over local rows [m0, m0 + M) (the kernel adds

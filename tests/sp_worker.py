@@ -1,6 +1,7 @@
 """Worker of tests/test_parallel_gpu.py (run under torchrun): the Ulysses engine on WORLD_SIZE GPUs against the
 single-GPU engine on the same seeded inputs and weights, over three forwards (dynamic, then delayed scales).  With
-SP_MASK=1 both engines run attention under the same seeded block-sparse mask."""
+SP_MASK=1 both engines run attention under the same seeded block-sparse mask; SP_QKV_PARTS=k splits the qkv GEMM and
+its exchange into k row parts (the engine's default otherwise)."""
 import os, sys
 from datetime import timedelta
 root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -23,6 +24,8 @@ rope = rope.reshape(1, S, 1, rot // 2, 2, 2).cuda()
 eng = M.MiniMaxH3Engine.synthetic(cfg, seed=1, device="cuda", group=dist.group.WORLD)
 mask = A.TileMask.block_sparse(S, keep=0.5, text_tokens=128, seed=3) if os.environ.get("SP_MASK") == "1" else None
 eng.attn_mask = mask
+if os.environ.get("SP_QKV_PARTS"):
+    eng.qkv_parts = int(os.environ["SP_QKV_PARTS"])
 n = S // world
 outs = []
 for f in range(3):

@@ -184,8 +184,8 @@ def test_shard_requires_even_split():
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
-@pytest.mark.parametrize("tile", [128, 2])   # 128: one GEMM launch at this n; 2: the two-row-half split
-def test_peer_store_layout_matches_all_to_all(world, tile):
+@pytest.mark.parametrize("tile,nparts", [(128, 2), (2, 2), (1, 4)])   # one launch at this n; two and four row parts
+def test_peer_store_layout_matches_all_to_all(world, tile, nparts):
     """The fused qkv exchange's addresses (tfvideo.parallel.QkvExchange, as the engine uses them) with the qkv
     GEMM's STORE_PEERS epilogue restated element by element (csrc/gemm_nvfp4.cuh: column (part, head, d) of launch
     row `row` goes to base[owner] + ((rank * M + row) * 3 + part) * Hr * 128 + (head % Hr) * 128 + d), then the
@@ -206,7 +206,8 @@ def test_peer_store_layout_matches_all_to_all(world, tile):
     local = [g.randn(n, 3, H, Dh).astype(np.float32) for _ in range(world)]
     for rank in range(world):
         xq = QkvExchange(rank, world, n, C, es, recv, send[rank])
-        parts = xq.row_parts(tile)
+        parts = xq.row_parts(tile, nparts)
+        assert len(parts) == (1 if tile == 128 else nparts)
         assert parts[0][0] == 0 and parts[-1][1] == n and all(a[1] == b[0] for a, b in zip(parts, parts[1:]))
         for r0, r1 in parts:
             M, base = r1 - r0, xq.bases(r0, r1 - r0)
