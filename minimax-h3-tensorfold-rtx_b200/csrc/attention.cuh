@@ -40,31 +40,58 @@ struct QkNormArgs {
 // rows.  Rows go in groups of eight (q and k of four heads), all eight loaded before any is written back: the rows
 // live in one buffer, so a load placed after a store could not be moved ahead of it, and one row in flight at a time
 // leaves the HBM pipe mostly idle.
-__device__ __forceinline__ uint2 qk_row(uint2 u, const float* w, const float (&f)[4][4], int lane, int half, int rot,
-                                        int src, float eps) {
-  float x[4] = {bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y)};
+//
+// Per group the sums of squares are reduced over the warp transposed: at each xor stage a lane sends the half of its
+// rows it gives up and adds the partner's half of the rows it keeps, so the five stages cost 9 shuffles for eight rows
+// instead of 40, and each lane ends with one row's sum (the same pairwise tree as a per-row xor butterfly, so the same
+// bits).  Each lane then takes one IEEE sqrt and division for that row and the eight 1/rms values are broadcast back.
+// The rotation is branch-free: a lane's four dims are all in the first half, all in the second, or all past `rot`, so
+// o = ca * y + cb * y_partner with per-lane coefficients (fp addition commutes, so f10 * y_i + f11 * y_j is the same
+// value in either order), and dims past `rot` keep y.
+__device__ __forceinline__ float sumsq4(uint2 u) {
+  const float x[4] = {bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y)};
   float ss = 0.f;
 #pragma unroll
   for (int e = 0; e < 4; ++e) ss = __fadd_rn(ss, __fmul_rn(x[e], x[e]));
+  return ss;
+}
+
+// p[j]: this lane's partial sum of row j -> the warp sum of row (4 (lane>>4 & 1) + 2 (lane>>3 & 1) + (lane>>2 & 1)).
+__device__ __forceinline__ float warp_sum8_transposed(const float (&p)[8], int lane) {
+  const bool b16 = lane & 16, b8 = lane & 8, b4 = lane & 4;
+  float q[4], r[2];
 #pragma unroll
-  for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), eps)));
+  for (int i = 0; i < 4; ++i) {
+    const float keep = b16 ? p[4 + i] : p[i], send = b16 ? p[i] : p[4 + i];
+    q[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 16));
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float keep = b8 ? q[2 + i] : q[i], send = b8 ? q[i] : q[2 + i];
+    r[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 8));
+  }
+  float s;
+  {
+    const float keep = b4 ? r[1] : r[0], send = b4 ? r[0] : r[1];
+    s = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+  }
+  s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 2));
+  s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 1));
+  return s;
+}
+
+__device__ __forceinline__ uint2 qk_row(uint2 u, const float* w, const float (&ca)[4], const float (&cb)[4],
+                                        bool rotated, int src, float r) {
+  const float x[4] = {bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y)};
   float y[4];
 #pragma unroll
   for (int e = 0; e < 4; ++e) y[e] = __fmul_rn(__fmul_rn(x[e], r), w[e]);
-  float pv[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) pv[e] = __shfl_sync(0xffffffffu, y[e], src);
   float o[4];
-  const int d0 = lane * 4;
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
-    if (d0 < half)
-      o[e] = __fadd_rn(__fmul_rn(f[e][0], y[e]), __fmul_rn(f[e][1], pv[e]));
-    else if (d0 < rot)
-      o[e] = __fadd_rn(__fmul_rn(f[e][2], pv[e]), __fmul_rn(f[e][3], y[e]));
-    else
-      o[e] = y[e];
+    const float pv = __shfl_sync(0xffffffffu, y[e], src);
+    const float t = __fadd_rn(__fmul_rn(ca[e], y[e]), __fmul_rn(cb[e], pv));
+    o[e] = rotated ? t : y[e];
   }
   return make_uint2(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]));
 }
@@ -75,20 +102,18 @@ __global__ void __launch_bounds__(256) qknorm_rope_kernel(QkNormArgs a) {
   if (s >= a.S) return;
   const int half = a.rot >> 1, hq = half >> 2;
   const int d0 = lane * 4;
-  int src = lane;
-  if (d0 < half) src = lane + hq;
-  else if (d0 < a.rot) src = lane - hq;
-  float f[4][4];
+  const bool first = d0 < half, rotated = d0 < a.rot;
+  const int src = first ? lane + hq : (rotated ? lane - hq : lane);
+  // o_i = f00 y_i + f01 y_j (first half), o_j = f11 y_j + f10 y_i (second half) for pair (i, j = i + rot/2)
+  float ca[4], cb[4];
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
     const int d = d0 + e;
-    const int pair = d < half ? d : d - half;
+    const int pair = first ? d : d - half;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (d < a.rot) v = *reinterpret_cast<const float4*>(a.rope + ((size_t)s * half + pair) * 4);
-    f[e][0] = v.x;
-    f[e][1] = v.y;
-    f[e][2] = v.z;
-    f[e][3] = v.w;
+    if (rotated) v = *reinterpret_cast<const float4*>(a.rope + ((size_t)s * half + pair) * 4);
+    ca[e] = first ? v.x : v.w;
+    cb[e] = first ? v.y : v.z;
   }
   float qw[4], kw[4];
 #pragma unroll
@@ -102,16 +127,25 @@ __global__ void __launch_bounds__(256) qknorm_rope_kernel(QkNormArgs a) {
     uint2 u[8];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
+      u[2 * j] = u[2 * j + 1] = make_uint2(0u, 0u);
       if (h0 + j < a.H) {
         u[2 * j] = *reinterpret_cast<const uint2*>(qrow + (h0 + j) * 128);
         u[2 * j + 1] = *reinterpret_cast<const uint2*>(krow + (h0 + j) * 128);
       }
     }
+    float p[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) p[j] = sumsq4(u[j]);
+    const float ss = warp_sum8_transposed(p, lane);
+    const float rmine = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), a.eps)));
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       if (h0 + j < a.H) {
-        *reinterpret_cast<uint2*>(qrow + (h0 + j) * 128) = qk_row(u[2 * j], qw, f, lane, half, a.rot, src, a.eps);
-        *reinterpret_cast<uint2*>(krow + (h0 + j) * 128) = qk_row(u[2 * j + 1], kw, f, lane, half, a.rot, src, a.eps);
+        const int kq = 2 * j, kk = 2 * j + 1;   // row k is held by lane 16 (k>>2) + 8 (k>>1 & 1) + 4 (k & 1)
+        const float rq = __shfl_sync(0xffffffffu, rmine, ((kq >> 2) << 4) | (((kq >> 1) & 1) << 3) | ((kq & 1) << 2));
+        const float rk = __shfl_sync(0xffffffffu, rmine, ((kk >> 2) << 4) | (((kk >> 1) & 1) << 3) | ((kk & 1) << 2));
+        *reinterpret_cast<uint2*>(qrow + (h0 + j) * 128) = qk_row(u[kq], qw, ca, cb, rotated, src, rq);
+        *reinterpret_cast<uint2*>(krow + (h0 + j) * 128) = qk_row(u[kk], kw, ca, cb, rotated, src, rk);
       }
     }
   }
