@@ -347,6 +347,36 @@ __device__ __forceinline__ uint32_t e2m1x8(const float* v) {
 
 // Quantise 16 consecutive values (already bf16-rounded, fp32) of one NVFP4 group under the global reciprocal
 // inv_g: returns the group's e4m3 scale byte and writes 8 code bytes (2 a byte, even element low) into `codes`.
+// 1 / max(e4m3(b), 1e-30) for a scale byte b in [0, 126], without a division.  A normal e4m3 value is
+// 2^(e - 7) (1 + m / 8), so its reciprocal is 2^(7 - e) * 8 / (8 + m): the correctly rounded fp32 of 8 / (8 + m),
+// scaled by an exact power of two.  A subnormal one is m / 512, reciprocal 512 / m, and byte 0 gives 1 / 1e-30.  The
+// sixteen constants are the correctly rounded quotients, so the result equals the IEEE division bit for bit
+// (checked on the GPU against __fdiv_rn for every byte).
+__device__ __forceinline__ float sel8(uint32_t m, uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint32_t c4,
+                                      uint32_t c5, uint32_t c6, uint32_t c7) {
+  const uint32_t a = (m & 1) ? c1 : c0, b = (m & 1) ? c3 : c2, d = (m & 1) ? c5 : c4, f = (m & 1) ? c7 : c6;
+  const uint32_t lo = (m & 2) ? b : a, hi = (m & 2) ? f : d;
+  return __uint_as_float((m & 4) ? hi : lo);
+}
+__device__ __forceinline__ float e4m3_rcp(uint32_t b) {
+  const uint32_t e = b >> 3, m = b & 7;
+  const float nrm = __fmul_rn(sel8(m, 0x3f800000u, 0x3f638e39u, 0x3f4ccccdu, 0x3f3a2e8cu, 0x3f2aaaabu, 0x3f1d89d9u,
+                                   0x3f124925u, 0x3f088889u),
+                              __uint_as_float((134u - e) << 23));
+  const float sub = sel8(m, 0x7149f2cau, 0x44000000u, 0x43800000u, 0x432aaaabu, 0x43000000u, 0x42cccccdu, 0x42aaaaabu,
+                         0x42924925u);
+  return e ? nrm : sub;
+}
+// x / 6 rounded to nearest even for x >= 0, without a division: q0 = x * RN(1/6), the exact remainder
+// r = x - 6 q0 by one fma, then q0 + r * RN(1/6) (Markstein's correction step for division by a known constant,
+// P. Markstein, "IA-64 and Elementary Functions", 2000).  Checked on the GPU against __fdiv_rn(x, 6) over every
+// non-negative finite fp32.
+__device__ __forceinline__ float div6_rn(float x) {
+  constexpr float c6 = 0.16666667163372039794921875f;   // RN(1/6) = 0x3e2aaaab
+  const float q0 = __fmul_rn(x, c6);
+  return __fmaf_rn(__fmaf_rn(-6.0f, q0, x), c6, q0);
+}
+
 __device__ __forceinline__ uint32_t quant_group16(const float (&v)[16], float inv_g, uint32_t (&codes)[2]) {
   float xs[16];
   float gmax = 0.f;
@@ -355,8 +385,8 @@ __device__ __forceinline__ uint32_t quant_group16(const float (&v)[16], float in
     xs[i] = __fmul_rn(v[i], inv_g);
     gmax = fmaxf(gmax, fabsf(xs[i]));
   }
-  uint32_t sf = e4m3(__fdiv_rn(gmax, 6.0f));
-  float inv = __fdiv_rn(1.0f, fmaxf(e4m3_to_f32(sf), 1e-30f));
+  uint32_t sf = e4m3(div6_rn(gmax));
+  float inv = e4m3_rcp(sf);
 #pragma unroll
   for (int i = 0; i < 16; ++i) xs[i] = __fmul_rn(xs[i], inv);
   codes[0] = e2m1x8(xs);
@@ -364,26 +394,6 @@ __device__ __forceinline__ uint32_t quant_group16(const float (&v)[16], float in
   return sf;
 }
 
-// quant_group16 with 1 / e4m3(scale) read from `rcp` (rcp[b] = the IEEE quotient 1 / max(e4m3(b), 1e-30) for the
-// scale bytes 0 .. 126 the saturating conversion can produce): the same codes, one division fewer per group.
-__device__ __forceinline__ uint32_t quant_group16_tab(const float (&v)[16], float inv_g, uint32_t (&codes)[2],
-                                                      const float* rcp) {
-  float xs[16];
-  float gmax = 0.f;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    xs[i] = __fmul_rn(v[i], inv_g);
-    gmax = fmaxf(gmax, fabsf(xs[i]));
-  }
-  uint32_t sf = e4m3(__fdiv_rn(gmax, 6.0f));
-  const float inv = rcp[sf];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) xs[i] = __fmul_rn(xs[i], inv);
-  codes[0] = e2m1x8(xs);
-  codes[1] = e2m1x8(xs + 8);
-  return sf;
-}
-__device__ __forceinline__ float e4m3_rcp_entry(uint32_t b) { return __fdiv_rn(1.0f, fmaxf(e4m3_to_f32(b), 1e-30f)); }
 
 // Byte offset of scale (row r, group k16) in the tiled scale layout the GEMM reads (128-row x 4-group atoms of 512
 // bytes, [row block][group block] order; inside an atom (r % 32) * 16 + (r / 32 % 4) * 4 + k16 % 4).

@@ -147,8 +147,8 @@ __global__ void __launch_bounds__(256) norm_mod_kernel(NormModArgs a) {
         gm = fmaxf(gm, fabsf(xs[j]));
       }
       gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 1));
-      uint32_t sfb = e4m3(__fdiv_rn(gm, 6.0f));
-      float inv = __fdiv_rn(1.0f, fmaxf(e4m3_to_f32(sfb), 1e-30f));
+      uint32_t sfb = e4m3(div6_rn(gm));
+      float inv = e4m3_rcp(sfb);
 #pragma unroll
       for (int j = 0; j < 8; ++j) xs[j] = __fmul_rn(xs[j], inv);
       uint32_t cw = e2m1x8(xs);
@@ -194,11 +194,8 @@ struct QuantArgs {
 
 __global__ void __launch_bounds__(256) nvfp4_quant_kernel(QuantArgs a) {
   const int groups = a.K >> 4;
-  // per block: the global scale's reciprocal and 1 / e4m3(scale) for every scale byte, the same IEEE divisions each
-  // group made before (170 against 176 us at [37,760, 5,120])
-  __shared__ float rcp_tab[128];
+  // the global scale's reciprocal once per block (one thread per group would otherwise divide per group)
   __shared__ float s_inv_g;
-  if (threadIdx.x < 128) rcp_tab[threadIdx.x] = e4m3_rcp_entry(threadIdx.x);
   if (threadIdx.x == 0) s_inv_g = __fdiv_rn(1.0f, a.g_ptr ? *a.g_ptr : a.g);
   __syncthreads();
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -220,7 +217,7 @@ __global__ void __launch_bounds__(256) nvfp4_quant_kernel(QuantArgs a) {
       am = fmaxf(am, fmaxf(fabsf(v[2 * j]), fabsf(v[2 * j + 1])));
     }
     uint32_t cw[2];
-    sfb = quant_group16_tab(v, s_inv_g, cw, rcp_tab);
+    sfb = quant_group16(v, s_inv_g, cw);
     *reinterpret_cast<uint2*>(a.codes + (size_t)r * (a.K >> 1) + (c >> 1)) = make_uint2(cw[0], cw[1]);
     off = a.sf_tiled ? sf_tiled_offset(r, k16, groups) : (size_t)r * groups + k16;
     if ((groups & 3) != 0) a.sf[off] = (uint8_t)sfb;
