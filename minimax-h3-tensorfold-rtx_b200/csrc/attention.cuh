@@ -80,6 +80,22 @@ __device__ __forceinline__ float warp_sum8_transposed(const float (&p)[8], int l
   return s;
 }
 
+// p[j]: this lane's partial max of row j -> the warp max of row (4 (lane>>4 & 1) + 2 (lane>>3 & 1) + (lane>>2 & 1)),
+// by the same transposed exchange (max is exact, so any order gives the same value)
+__device__ __forceinline__ float warp_max8_transposed(const float (&p)[8], int lane) {
+  const bool b16 = lane & 16, b8 = lane & 8, b4 = lane & 4;
+  float q[4], r[2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    q[i] = fmaxf(b16 ? p[4 + i] : p[i], __shfl_xor_sync(0xffffffffu, b16 ? p[i] : p[4 + i], 16));
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    r[i] = fmaxf(b8 ? q[2 + i] : q[i], __shfl_xor_sync(0xffffffffu, b8 ? q[i] : q[2 + i], 8));
+  float s = fmaxf(b4 ? r[1] : r[0], __shfl_xor_sync(0xffffffffu, b4 ? r[0] : r[1], 4));
+  s = fmaxf(s, __shfl_xor_sync(0xffffffffu, s, 2));
+  return fmaxf(s, __shfl_xor_sync(0xffffffffu, s, 1));
+}
+
 __device__ __forceinline__ uint2 qk_row(uint2 u, const float* w, const float (&ca)[4], const float (&cb)[4],
                                         bool rotated, int src, float r) {
   const float x[4] = {bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y)};
@@ -208,9 +224,23 @@ __global__ void attn_stats_reduce_kernel(const float* ksum_part, const float* vm
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= H * 128) return;
   float ks = 0.f, vm = 0.f;
-  for (int b = 0; b < nblk; ++b) {
-    ks = __fadd_rn(ks, ksum_part[(size_t)b * H * 128 + i]);
-    vm = fmaxf(vm, vmax_part[(size_t)b * H * 128 + i]);
+  // eight blocks' partials are loaded before any is added (one load in flight at a time made this a chain of
+  // memory latencies, 43 us at S = 37,760); the sum keeps its block order
+  for (int b0 = 0; b0 < nblk; b0 += 8) {
+    float kp[8], vp[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const bool in = b0 + j < nblk;
+      kp[j] = in ? ksum_part[(size_t)(b0 + j) * H * 128 + i] : 0.f;
+      vp[j] = in ? vmax_part[(size_t)(b0 + j) * H * 128 + i] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (b0 + j < nblk) {
+        ks = __fadd_rn(ks, kp[j]);
+        vm = fmaxf(vm, vp[j]);
+      }
+    }
   }
   kmean[i] = __fdiv_rn(ks, (float)S);
   vm = fmaxf(vm, 1e-30f);
@@ -247,23 +277,32 @@ __global__ void __launch_bounds__(128) attn_quant_kernel(AttnView a, int S, int 
     return e4m3x2(__fmul_rn(y[0], inv), __fmul_rn(y[1], inv)) |
            (e4m3x2(__fmul_rn(y[2], inv), __fmul_rn(y[3], inv)) << 16);
   };
-  // ---- Q: one fp32 scale per row
-#pragma unroll 4
-  for (int i = 0; i < 32; ++i) {
-    const int t = blk * 128 + warp * 32 + i;
-    float x[4];
-    load4(a.q, t, x);
-    float amax = 0.f;
+  // ---- Q: one fp32 scale per row, eight rows at a time: the row maxima are reduced transposed (each lane ends with
+  // one row's max), so each lane makes the scale's two IEEE divisions for one row instead of all lanes for every row
+#pragma unroll 1
+  for (int i0 = 0; i0 < 32; i0 += 8) {
+    const int t0 = blk * 128 + warp * 32 + i0;
+    float x[8][4], pm[8];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      x[j] = __fmul_rn(x[j], qmul);
-      amax = fmaxf(amax, fabsf(x[j]));
+    for (int r = 0; r < 8; ++r) {
+      load4(a.q, t0 + r, x[r]);
+      pm[r] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        x[r][j] = __fmul_rn(x[r][j], qmul);
+        pm[r] = fmaxf(pm[r], fabsf(x[r][j]));
+      }
     }
-    amax = warp_max(amax);
-    const float qr = __fdiv_rn(fmaxf(amax, 1e-30f), 448.0f);
-    const uint32_t w = pack4(x, __fdiv_rn(1.0f, qr));
-    reinterpret_cast<uint32_t*>(q8 + ((size_t)h * SP + t) * 128)[lane] = w;
-    if (lane == 0) qscale[(size_t)h * SP + t] = qr;   // tiny but finite for padded rows: no NaN from masked keys
+    const int mine = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);   // the row this lane ends with
+    const float qr_mine = __fdiv_rn(fmaxf(warp_max8_transposed(pm, lane), 1e-30f), 448.0f);
+    const float qi_mine = __fdiv_rn(1.0f, qr_mine);
+    if ((lane & 3) == 0) qscale[(size_t)h * SP + t0 + mine] = qr_mine;   // tiny but finite for padded rows
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int src = ((r >> 2) << 4) | (((r >> 1) & 1) << 3) | ((r & 1) << 2);
+      const float qi = __shfl_sync(0xffffffffu, qi_mine, src);
+      reinterpret_cast<uint32_t*>(q8 + ((size_t)h * SP + t0 + r) * 128)[lane] = pack4(x[r], qi);
+    }
   }
   // ---- K (smoothed by the sequence mean, one scale per 128-key block)
   float km[4];
