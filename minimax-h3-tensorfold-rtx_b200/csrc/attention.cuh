@@ -21,9 +21,9 @@ namespace h3 {
 constexpr float kLog2e = 1.4426950408889634f;
 
 // ------------------------------------------------------------------------------------------------ qk norm + rope
-// One warp per (token, q|k, head) row of Dh = 128; lane l owns dims 4l..4l+3.  y = x / sqrt(mean(x^2) + eps) * w;
-// pair i < rot/2 couples dims i and i + rot/2 through the token's 2x2 matrix rope[s, i] (o_i = f00 y_i + f01 y_j,
-// o_j = f10 y_i + f11 y_j); dims >= rot pass through.  In place on the bf16 rows.
+// Per (token, q|k, head) row of Dh = 128, lane l of the token's warp owns dims 4l..4l+3.
+// y = x / sqrt(mean(x^2) + eps) * w; pair i < rot/2 couples dims i and i + rot/2 through the token's 2x2 matrix
+// rope[s, i] (o_i = f00 y_i + f01 y_j, o_j = f10 y_i + f11 y_j); dims >= rot pass through.  In place on the bf16 rows.
 struct QkNormArgs {
   __nv_bfloat16* q;      // element (s, h, d) at q + s * ld + h * 128 + d
   __nv_bfloat16* k;

@@ -14,6 +14,8 @@ samples query rows; its bar for bf16-class outputs is cosine >= 0.998, AGENTS.md
   * config 0 -- one block, S = 4096, D = 5120, 40 x 128 heads, GELU 20480, through EngineBlock: cosine >= 0.998
     against the oracle's bf16 / SDPA block (all rows); the NVFP4 codes the block itself wrote for its fc1 and fc2
     inputs bit-exact against the oracle quantiser at that shape.
+  * the real MiniMax H3 shape the drop-in serves -- one block, S = 1024, D = 5376, 56 x 128 heads, SwiGLU 14336,
+    RoPE over 96 dims: cosine >= 0.998 against the oracle's bf16 / SDPA block.
 
 Inputs are made on the device from seeded generators with BASELINE's distributions (activations N(0, 1) with 1% of
 channels x 20, weights N(0, 0.02)); only the sampled rows and the operands the oracle needs come back to the host.
@@ -238,6 +240,39 @@ def test_config0_block_s4096():
         assert np.array_equal(ON.sf_from_tiled(u8(sf), S, a.shape[1] // 16), rsf), f"{name}: scales differ"
     # the block against the oracle's bf16 / fp32-SDPA block (the north star's bar)
     shape = OB.BlockShape(dim=cfg.dim, heads=cfg.heads, head_dim=cfg.head_dim, ffn=cfg.ffn, act="gelu", rot_dim=128)
+    p = OB.BlockParams(w={n: to_np(w[n]) for n in ("qkv", "out", "fc1", "fc2")}, norm1=to_np(w["norm1"]),
+                       norm2=to_np(w["norm2"]), q_norm=to_np(w["q_norm"]), k_norm=to_np(w["k_norm"]),
+                       ada_w=to_np(w["ada_w"]), ada_b=to_np(w["ada_b"]))
+    del w
+    ref = OB.block_forward(shape, p, x_np, t_emb.numpy(), segs, rope, linears="bf16", attn="sdpa")
+    c = OO.cosine(out, ref)
+    cu = OO.cosine(out - x_np, ref - x_np)
+    assert c >= COS_BAR, f"block cosine {c:.6f}"
+    assert cu >= 0.95, f"block update cosine {cu:.6f}"
+
+
+# ------------------------------------------------------------------------------------------------ real H3 shape
+def test_h3_shape_block_s1024():
+    """One block at the real MiniMax H3 shape the drop-in serves (tfvideo/minimax_h3.py:28-36: D 5376, 56 x 128 heads,
+    SwiGLU 14336, RoPE over 96 dims) against the oracle's bf16 / fp32-SDPA block, two modulation segments."""
+
+    from tfvideo import minimax_h3 as M
+
+    S = 1024
+    cfg = M.Config(layers=1)
+    assert (cfg.dim, cfg.heads, cfg.ffn, cfg.act) == (5376, 56, 14336, "swiglu")
+    w = next(M.synthetic_weights(cfg, seed=21, device="cuda"))
+    eng = M.MiniMaxH3Engine.from_weights([w], cfg, device="cuda")
+    x = dev_activations(S, cfg.dim, seed=22)
+    x_np = to_np(x)
+    t_emb = torch.randn(2, cfg.t_dim, generator=torch.Generator().manual_seed(23))
+    segs = [(0, 256, 0), (256, S, 1)]
+    rope = OB.rope_table(S, 96)
+    rope_t = torch.from_numpy(rope).cuda().reshape(1, S, 1, 48, 2, 2)
+    out = to_np(M.EngineBlock(eng, 0)(x, t_emb.cuda(), segs, rope_t))
+    device_ok()
+    assert np.isfinite(out).all()
+    shape = OB.BlockShape(dim=cfg.dim, heads=cfg.heads, head_dim=cfg.head_dim, ffn=cfg.ffn, act="swiglu", rot_dim=96)
     p = OB.BlockParams(w={n: to_np(w[n]) for n in ("qkv", "out", "fc1", "fc2")}, norm1=to_np(w["norm1"]),
                        norm2=to_np(w["norm2"]), q_norm=to_np(w["q_norm"]), k_norm=to_np(w["k_norm"]),
                        ada_w=to_np(w["ada_w"]), ada_b=to_np(w["ada_b"]))
