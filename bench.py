@@ -515,6 +515,8 @@ def main():
     ap.add_argument("--micro", choices=["attn", "gemm", "elem"],
                     help="time one op alone (BASELINE configs 1 / 2; elem: the HBM-bound kernels)")
     ap.add_argument("--heads", type=int, default=40)
+    ap.add_argument("--copy-streams", type=int, default=None,
+                    help="Ulysses: side streams for the qkv exchange copies (engine default)")
     ap.add_argument("--qkv-parts", type=int, default=None,
                     help="Ulysses: row parts of the qkv GEMM whose exchange overlaps the next part (engine default)")
     ap.add_argument("--mnk", default="37760,15360,5120", help="--micro gemm: M,N,K")
@@ -551,6 +553,8 @@ def main():
         eng.attn_mask = A.TileMask.block_sparse(S)
     if a.qkv_parts:
         eng.qkv_parts = a.qkv_parts
+    if a.copy_streams:
+        eng.copy_streams = a.copy_streams
     x0 = activations(S, cfg.dim)[t0:t0 + n].cuda()
     t_emb = torch.randn(2, cfg.t_dim, generator=torch.Generator().manual_seed(3)).cuda()
     segs = mod_segments(S)

@@ -158,6 +158,7 @@ class MiniMaxH3Engine:
         self.timer = None                  # a profiling.StageTimer to time each stage of each block
         self.attn_mask = None              # attention.TileMask: block-sparse FP8 attention when set
         self.qkv_parts = 4                 # Ulysses: row parts of the qkv GEMM (all but the last sent by copy engines)
+        self.copy_streams = 7              # Ulysses: side streams for those copies (one per destination rank at 8)
 
     # ------------------------------------------------------------------ construction
     @classmethod
@@ -341,9 +342,12 @@ class MiniMaxH3Engine:
             qp, op = buf.peers
             xq = QkvExchange(rank, world, n, 3 * Hl * Dh, buf.qkv.element_size(), qp.ptrs, buf.qkv.data_ptr())
             # row parts: each part's blocks but the last leave on the copy engines (no SMs) while the GEMM computes
-            # the next part; the last part's go by the push kernel once the GEMM has freed the SMs
+            # the next part, one side stream per destination rank so that the copies to different ranks run on
+            # different copy engines at once; the last part's go by the push kernel once the GEMM has freed the SMs
             parts = xq.row_parts(parts=self.qkv_parts)
-            side = self.__dict__.setdefault("_side_stream", torch.cuda.Stream(device=self.device))
+            sides = self.__dict__.setdefault(
+                "_side_streams", [torch.cuda.Stream(device=self.device) for _ in range(max(1, self.copy_streams))])
+            cur = torch.cuda.current_stream(self.device)
             with maybe(T, "gemm_qkv"):
                 for j, (r0, r1) in enumerate(parts):
                     epi = N.H3Epilogue(kind=N.H3_EPI_STORE_PEERS, ranks=world, rank=rank)
@@ -351,11 +355,14 @@ class MiniMaxH3Engine:
                         epi.peer[r] = pp
                     lq.gemm(buf.h4[r0:r1], buf.h4sf[N.sf_tiled_bytes(r0, D) if r0 else 0:], r1 - r0, epi)
                     if j + 1 < len(parts):
-                        side.wait_stream(torch.cuda.current_stream(self.device))
-                        N.peer_copy(xq.copies(r0, r1), side.cuda_stream)
+                        for c, copy in enumerate(xq.copies(r0, r1)):
+                            side = sides[c % len(sides)]
+                            side.wait_stream(cur)
+                            N.peer_copy([copy], side.cuda_stream)
             with maybe(T, "exchange_push"):
                 N.peer_push(xq.copies(*parts[-1]))
-                torch.cuda.current_stream(self.device).wait_stream(side)
+                for side in sides:
+                    cur.wait_stream(side)
             with maybe(T, "exchange_barrier"):
                 self.sp.barrier(self.device)
             qa = buf.qkv_all.view(S, 3 * Hl * Dh)
