@@ -515,6 +515,8 @@ def main():
     ap.add_argument("--micro", choices=["attn", "gemm", "elem"],
                     help="time one op alone (BASELINE configs 1 / 2; elem: the HBM-bound kernels)")
     ap.add_argument("--heads", type=int, default=40)
+    ap.add_argument("--part-sender", choices=["copy", "push", "auto"], default=None,
+                    help="Ulysses: how the qkv parts but the last are sent while the GEMM runs (engine default)")
     ap.add_argument("--copy-streams", type=int, default=None,
                     help="Ulysses: side streams for the qkv exchange copies (engine default)")
     ap.add_argument("--qkv-parts", type=int, default=None,
@@ -555,6 +557,8 @@ def main():
         eng.qkv_parts = a.qkv_parts
     if a.copy_streams:
         eng.copy_streams = a.copy_streams
+    if a.part_sender:
+        eng.part_sender = a.part_sender
     x0 = activations(S, cfg.dim)[t0:t0 + n].cuda()
     t_emb = torch.randn(2, cfg.t_dim, generator=torch.Generator().manual_seed(3)).cuda()
     segs = mod_segments(S)

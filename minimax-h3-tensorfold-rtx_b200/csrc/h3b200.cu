@@ -331,10 +331,12 @@ int h3_peer_push(const H3PeerCopy* copies, int n, void* stream) {
     most = a.n16[c] > most ? a.n16[c] : most;
   }
   if (most == 0) return H3_OK;
-  long long blocks = (most + 1023) / 1024;
-  const long long cap = 2LL * num_sms();   // per copy; n copies share the SMs
+  // about one 128-thread block (6 K registers) per SM over all n copies: one fits beside a persistent GEMM CTA on
+  // its SM, so a push issued on a side stream runs while the GEMM computes the next rows
+  long long blocks = (most + 511) / 512;
+  const long long cap = num_sms() / n > 0 ? num_sms() / n : 1;   // per copy
   if (blocks > cap) blocks = cap;
-  peer_push_kernel<<<dim3((unsigned)blocks, n), 256, 0, S_(stream)>>>(a);
+  peer_push_kernel<<<dim3((unsigned)blocks, n), 128, 0, S_(stream)>>>(a);
   return check_launch("h3_peer_push");
 }
 

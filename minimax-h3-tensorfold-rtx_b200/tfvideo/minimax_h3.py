@@ -159,6 +159,8 @@ class MiniMaxH3Engine:
         self.attn_mask = None              # attention.TileMask: block-sparse FP8 attention when set
         self.qkv_parts = 4                 # Ulysses: row parts of the qkv GEMM (all but the last sent by copy engines)
         self.copy_streams = 7              # Ulysses: side streams for those copies (one per destination rank at 8)
+        self.part_sender = "auto"          # Ulysses: "copy" (copy engines), "push" (a push kernel beside the GEMM),
+                                           # "auto": push at 8 or more ranks, where it measured faster, else copy
 
     # ------------------------------------------------------------------ construction
     @classmethod
@@ -355,10 +357,17 @@ class MiniMaxH3Engine:
                         epi.peer[r] = pp
                     lq.gemm(buf.h4[r0:r1], buf.h4sf[N.sf_tiled_bytes(r0, D) if r0 else 0:], r1 - r0, epi)
                     if j + 1 < len(parts):
-                        for c, copy in enumerate(xq.copies(r0, r1)):
-                            side = sides[c % len(sides)]
-                            side.wait_stream(cur)
-                            N.peer_copy([copy], side.cuda_stream)
+                        sender = self.part_sender
+                        if sender == "auto":
+                            sender = "push" if world >= 8 else "copy"
+                        if sender == "push":    # one push kernel beside the GEMM's next part
+                            sides[0].wait_stream(cur)
+                            N.peer_push(xq.copies(r0, r1), sides[0].cuda_stream)
+                        else:
+                            for c, copy in enumerate(xq.copies(r0, r1)):
+                                side = sides[c % len(sides)]
+                                side.wait_stream(cur)
+                                N.peer_copy([copy], side.cuda_stream)
             with maybe(T, "exchange_push"):
                 N.peer_push(xq.copies(*parts[-1]))
                 for side in sides:

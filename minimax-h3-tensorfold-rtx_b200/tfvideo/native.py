@@ -262,12 +262,13 @@ def peer_open(handle: bytes) -> int:
     return p.value
 
 
-def peer_push(copies: list[tuple[int, int, int]]) -> None:
-    """(src, dst, bytes) contiguous copies in one kernel on the current stream, e.g. into other ranks' buffers."""
+def peer_push(copies: list[tuple[int, int, int]], stream_handle: int | None = None) -> None:
+    """(src, dst, bytes) contiguous copies in one kernel, e.g. into other ranks' buffers, on torch's current stream
+    unless given."""
 
     _count(1)
     arr = (H3PeerCopy * len(copies))(*[H3PeerCopy(s, d, b) for s, d, b in copies])
-    check(lib().h3_peer_push(arr, len(copies), stream()), "h3_peer_push")
+    check(lib().h3_peer_push(arr, len(copies), stream() if stream_handle is None else stream_handle), "h3_peer_push")
 
 
 def peer_copy(copies: list[tuple[int, int, int]], stream_handle: int | None = None) -> None:

@@ -1,7 +1,8 @@
 """Worker of tests/test_parallel_gpu.py (run under torchrun): the Ulysses engine on WORLD_SIZE GPUs against the
 single-GPU engine on the same seeded inputs and weights, over three forwards (dynamic, then delayed scales).  With
 SP_MASK=1 both engines run attention under the same seeded block-sparse mask; SP_QKV_PARTS=k splits the qkv GEMM and
-its exchange into k row parts (the engine's default otherwise)."""
+its exchange into k row parts and SP_PART_SENDER=copy|push picks how the parts are sent (the engine's defaults
+otherwise)."""
 import os, sys
 from datetime import timedelta
 root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -26,6 +27,8 @@ mask = A.TileMask.block_sparse(S, keep=0.5, text_tokens=128, seed=3) if os.envir
 eng.attn_mask = mask
 if os.environ.get("SP_QKV_PARTS"):
     eng.qkv_parts = int(os.environ["SP_QKV_PARTS"])
+if os.environ.get("SP_PART_SENDER"):
+    eng.part_sender = os.environ["SP_PART_SENDER"]
 n = S // world
 outs = []
 for f in range(3):
