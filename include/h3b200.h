@@ -139,8 +139,10 @@ typedef struct H3PeerCopy {
   size_t bytes;
 } H3PeerCopy;
 /* Up to 8 copies in one kernel, typically into other ranks' peer buffers: every warp stores 512 contiguous bytes at a
- * time, so writes to another GPU cross NVLink in full packets (row-scattered 16-byte stores do not).  Like any
- * kernel's, its writes are visible to work ordered after its completion (for another rank: after a barrier). */
+ * time, so writes to another GPU cross NVLink in full packets (row-scattered 16-byte stores do not).  The grid is
+ * about one 128-thread block per SM over all copies, small enough to sit beside a persistent h3_gemm_nvfp4 CTA, so a
+ * push on another stream runs while the GEMM does.  Like any kernel's, its writes are visible to work ordered after
+ * its completion (for another rank: after a barrier). */
 int h3_peer_push(const H3PeerCopy* copies, int n, void* stream);
 /* The same copies (any number) as cudaMemcpyAsync device-to-device calls on `stream`, one per copy: the copy engines
  * move the data, so it overlaps kernels that hold every SM (a persistent GEMM). */
